@@ -1,0 +1,551 @@
+#!/usr/bin/env python
+"""Benchmark of the cufk reconstruction hot path on B200: fwd+bwd atoms/s (B=4096, N=768, fp32).
+
+One step = the block forward plus the block backward over this rank's shard of config 1
+(B = 4096 chains split evenly over the ranks, N = 768 atoms, float32).  Prints ONE JSON line on
+rank 0.
+
+* ``value``: atoms of all ranks / (max over ranks of the device time per step).  Inputs are
+  resident in HBM.  Each step replays a CUDA graph holding the two kernel launches for one of
+  several input sets; the sets rotate so that the data of a step was last touched several steps
+  earlier (total footprint > 3x the 126 MB L2), i.e. every step reads its inputs from HBM.
+* ``roofline``: algorithmic bytes per launch (forward 24 B/atom, backward 36 B/atom in fp32, from
+  the minimum reads and writes) / the average launch duration of that kernel, timed with CUDA
+  events in a second region of single-kernel graphs; ``peak`` from MEASURED_PEAKS.json.
+* ``e2e``: the same metric through the public API (``cufk_b200.reconstruct`` + autograd) with
+  pinned host buffers: every step copies its inputs host->device and its outputs device->host.
+* ``cpu_baseline``: the float64 torch restatement (oracle/nerf64.py) on the host cores, on a
+  bounded sample of the same workload (rank 0, single-GPU runs only).
+* ``--impl reference``: the reference arm.  The reference's path exists only as CUDA kernels, so
+  the CPU implementation timed is the float64 restatement of its algorithm on all host cores.
+
+Multi-GPU: ``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``; the batch
+is sharded by chains with no collective on the hot path (strong scaling of the fixed B = 4096);
+an NCCL all-gather of xyz is timed separately and reported under ``allgather``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "fwd+bwd atoms/s (B=4096,N=768 fp32)"
+GLOBAL_BATCH = 4096
+POINTS = 768
+L2_BYTES = 126 * 1024 * 1024
+HBM_FALLBACK_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global number of chains")
+    ap.add_argument("--points", type=int, default=POINTS)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ------------------------------------------------------------------------------------------------
+# distributed plumbing
+# ------------------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self, gpus: int, device_needed: bool = True):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != gpus and self.world > 1:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            if device_needed:
+                torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(
+                "nccl" if device_needed else "gloo",
+                timeout=datetime.timedelta(seconds=120),
+                device_id=torch.device("cuda", self.local_rank) if device_needed else None,
+            )
+            self.pg = dist
+        elif device_needed:
+            torch.cuda.set_device(0)
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def make_inputs(batch: int, points: int, seed: int = 0) -> dict:
+    """Seeded synthetic config-1 inputs (float64 on the CPU, cast to float32).
+
+    lengths cycle the backbone bond lengths (0.14685231, 0.15365194, 0.13405086) nm + N(0, 0.002);
+    angles cycle (1.9676635, 2.062335, 2.164016) rad + N(0, 0.03); dihedrals ~ U(-pi, pi);
+    grad_out ~ N(0, 1).  No public dataset exists for this path; these are the benchmark inputs.
+    """
+    g = torch.Generator().manual_seed(seed)
+    f64 = torch.float64
+    i1 = torch.arange(points - 1)
+    i2 = torch.arange(points - 2)
+    L = torch.tensor((0.14685231, 0.15365194, 0.13405086), dtype=f64)[i1 % 3] + 0.002 * torch.randn(batch, points - 1, generator=g, dtype=f64)
+    A = torch.tensor((1.9676635, 2.062335, 2.164016), dtype=f64)[i2 % 3] + 0.03 * torch.randn(batch, points - 2, generator=g, dtype=f64)
+    D = (torch.rand(batch, points - 3, generator=g, dtype=f64) * 2.0 - 1.0) * math.pi
+    G = torch.randn(batch, points, 3, generator=g, dtype=f64)
+    return {"lengths": L.float(), "angles": A.float(), "dihedrals": D.float(), "grad": G.float()}
+
+
+def shard(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous chain range [lo, hi) of this rank (chains are independent: no exchange)."""
+    per, extra = divmod(batch, world)
+    lo = rank * per + min(rank, extra)
+    return lo, lo + per + (1 if rank < extra else 0)
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks: NVML sampling during the timed region (read-only queries)
+# ------------------------------------------------------------------------------------------------
+REASON_BITS = {
+    0x4: "sw_power_cap",
+    0x8: "hw_slowdown",
+    0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown",
+    0x2: "applications_clocks_setting",
+    0x10: "sync_boost",
+}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.handle = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+        except Exception as exc:  # noqa: BLE001 - clocks are reported as unavailable
+            self.error = repr(exc)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "error", "nvml unavailable")}
+        names = sorted(name for bit, name in REASON_BITS.items() if self.reasons & bit)
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "samples": len(self.samples),
+        }
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def bytes_per_atom(points: int, elem: int = 4) -> tuple[float, float]:
+    """Algorithmic bytes per chain / N: forward reads 3N-6, writes 3N; backward reads 3N-6 + 3N,
+    writes 3N-6 elements."""
+    fwd = (6 * points - 6) * elem / points
+    bwd = (9 * points - 12) * elem / points
+    return fwd, bwd
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        if data.get("hbm_gbs"):
+            return float(data["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def profiled_traffic_per_atom(kernel: str):
+    """DRAM bytes per atom of one launch from the committed ncu summary (profiles/traffic.json)."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(kernel)
+    return None if entry is None else float(entry["dram_bytes_per_atom"])
+
+
+def time_graphs(graphs, steps: int, warmup: int, dist: Dist, stream) -> float:
+    """Replays graphs[k % len] for `warmup` then `steps` iterations; returns max-over-ranks ms."""
+    for k in range(warmup):
+        graphs[k % len(graphs)].replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(steps):
+        graphs[k % len(graphs)].replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    return dist.max(start.elapsed_time(end))
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    sys.path.insert(0, str(ROOT))
+    import cufk_b200 as cufk
+    from cufk_b200 import _native
+
+    C = _native._C
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lo, hi = shard(args.batch, dist.world, dist.rank)
+    b_local = hi - lo
+    n = args.points
+
+    # synthetic config-1 inputs: the global batch is generated identically on every rank from seed 0
+    host = make_inputs(args.batch, n, seed=0)
+    host = {k: v[lo:hi].contiguous() for k, v in host.items()}
+    set_bytes = 4 * b_local * ((n - 1) + (n - 2) + (n - 3) + 3 * n) * 2  # inputs + outputs of a step
+    n_sets = max(2, min(64, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
+    sets = []
+    for i in range(n_sets):
+        # each set a distinct copy (perturbed dihedrals) so no two sets alias
+        d = {k: v.to(dev) for k, v in host.items()}
+        d["dihedrals"] = d["dihedrals"] + 1e-3 * i
+        sets.append(d)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graphs_step, graphs_fwd, graphs_bwd = [], [], []
+    with torch.cuda.stream(stream):
+        for d in sets:  # eager warm-up of both kernels (first-call attribute setup happens here)
+            C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+            C.block_backward(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["grad"])
+        stream.synchronize()
+        for d in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                C.block_backward(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["grad"])
+            graphs_step.append(g)
+            gf = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gf, stream=stream):
+                C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+            graphs_fwd.append(gf)
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gb, stream=stream):
+                C.block_backward(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["grad"])
+            graphs_bwd.append(gb)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(dev.index)
+    with torch.cuda.stream(stream):
+        with sampler:
+            ms_total = time_graphs(graphs_step, args.steps, args.warmup, dist, stream)
+        ms_fwd = time_graphs(graphs_fwd, args.steps, args.warmup, dist, stream) / args.steps
+        ms_bwd = time_graphs(graphs_bwd, args.steps, args.warmup, dist, stream) / args.steps
+    ms_step = ms_total / args.steps
+    atoms_total = args.batch * n
+    value = atoms_total / (ms_step * 1e-3)
+
+    # roofline of the dominant kernel
+    peak, peak_kind = measured_peak()
+    fwd_bpa, bwd_bpa = bytes_per_atom(n)
+    atoms_local = b_local * n
+    per_kernel = {
+        "block_forward_kernel": (ms_fwd, fwd_bpa),
+        "block_backward_kernel": (ms_bwd, bwd_bpa),
+    }
+    dom = max(per_kernel, key=lambda k: per_kernel[k][0])
+    ms_dom, bpa_dom = per_kernel[dom]
+    achieved = bpa_dom * atoms_local / (ms_dom * 1e-3) / 1e9
+    traffic_pa = profiled_traffic_per_atom(dom)
+    roofline = {
+        "kernel": dom,
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+        "traffic": None if traffic_pa is None else round(traffic_pa * atoms_local),
+        "algorithmic_bytes": round(bpa_dom * atoms_local),
+        "launch_ms": round(ms_dom, 5),
+        "per_kernel": {
+            k: {
+                "launch_ms": round(t, 5),
+                "bytes_per_atom": round(b, 3),
+                "achieved_gbs": round(b * atoms_local / (t * 1e-3) / 1e9, 1),
+                "frac": round(b * atoms_local / (t * 1e-3) / 1e9 / peak, 4),
+            }
+            for k, (t, b) in per_kernel.items()
+        },
+        "step_frac": round((fwd_bpa + bwd_bpa) * atoms_local / (ms_step * 1e-3) / 1e9 / peak, 4),
+    }
+
+    # optional NCCL all-gather of xyz (not part of the step), timed separately
+    allgather = None
+    if dist.world > 1:
+        xyz = torch.empty(b_local, n, 3, device=dev)
+        full = torch.empty(b_local * dist.world, n, 3, device=dev)
+        for _ in range(3):
+            dist.pg.all_gather_into_tensor(full, xyz)
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps = 20
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            dist.pg.all_gather_into_tensor(full, xyz)
+        s1.record()
+        torch.cuda.synchronize()
+        ms_ag = dist.max(s0.elapsed_time(s1) / reps)
+        nbytes = full.numel() * 4
+        allgather = {
+            "ms": round(ms_ag, 4),
+            "bytes": nbytes,
+            "bus_gbs": round(nbytes * (dist.world - 1) / dist.world / (ms_ag * 1e-3) / 1e9, 1),
+        }
+
+    # end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(cufk, host, dev, args, dist)
+
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "atoms/s",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded backbone internal coordinates, oracle/nerf64.make_inputs)",
+        "config": {
+            "workload": "config 1: block reconstruct forward+backward, B=4096 chains (global), N=768 atoms, fp32",
+            "global_batch": args.batch,
+            "points": n,
+            "per_gpu_batch": b_local,
+            "parallelism": f"batch-sharded x{dist.world}, no collective on the hot path",
+            "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB > L2 (126 MB)",
+            "timing": "one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks",
+        },
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if allgather is not None:
+        result["allgather"] = allgather
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(n)
+    return result
+
+
+def run_e2e(cufk, host, dev, args, dist: Dist) -> dict:
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    outs = {
+        "xyz": torch.empty(host["lengths"].shape[0], args.points, 3).pin_memory(),
+        "gl": torch.empty_like(host["lengths"]).pin_memory(),
+        "ga": torch.empty_like(host["angles"]).pin_memory(),
+        "gd": torch.empty_like(host["dihedrals"]).pin_memory(),
+    }
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values())
+    d2h = sum(v.numel() * v.element_size() for v in outs.values())
+
+    def step():
+        L = pinned["lengths"].to(dev, non_blocking=True).requires_grad_(True)
+        A = pinned["angles"].to(dev, non_blocking=True).requires_grad_(True)
+        D = pinned["dihedrals"].to(dev, non_blocking=True).requires_grad_(True)
+        G = pinned["grad"].to(dev, non_blocking=True)
+        xyz = cufk.reconstruct(L, A, D)
+        xyz.backward(G)
+        outs["xyz"].copy_(xyz.detach(), non_blocking=True)
+        outs["gl"].copy_(L.grad, non_blocking=True)
+        outs["ga"].copy_(A.grad, non_blocking=True)
+        outs["gd"].copy_(D.grad, non_blocking=True)
+
+    steps = min(args.steps, 100)
+    for _ in range(max(3, min(args.warmup, 10))):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        step()
+    s1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(s0.elapsed_time(s1)) / steps
+    return {
+        "value": args.batch * args.points / (ms * 1e-3),
+        "unit": "atoms/s",
+        "h2d_bytes_per_step": h2d,
+        "d2h_bytes_per_step": d2h,
+        "ms_per_step": ms,
+        "steps": steps,
+        "path": "cufk_b200.reconstruct + autograd backward; pinned host buffers, copies inside the timed region",
+    }
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline and the reference arm: the float64 restatement on the host cores
+# ------------------------------------------------------------------------------------------------
+def _cpu_sample(points: int, chains: int):
+    from oracle import nerf64
+
+    inp = make_inputs(chains, points, seed=1)
+
+    def once():
+        nerf64.reconstruct64_with_grads(inp["lengths"], inp["angles"], inp["dihedrals"], inp["grad"])
+
+    return once
+
+
+def cpu_baseline(points: int, budget_s: float = 12.0, chains: int = 256) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    once = _cpu_sample(points, chains)
+    once()  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        once()
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {
+        "value": chains * points / dt,
+        "unit": "atoms/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{chains} chains x N={points} fwd+bwd (float64 torch, autograd backward), {reps} reps in {budget_s:.0f}s",
+    }
+
+
+def run_reference(args) -> dict | None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sys.path.insert(0, str(ROOT))
+    torch.set_num_threads(os.cpu_count() or 1)
+    chains = 64
+    once = _cpu_sample(args.points, chains)
+    for _ in range(max(1, args.warmup)):
+        once()
+    steps = args.steps
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        once()
+    dt = (time.perf_counter() - t0) / steps
+    value = chains * args.points / dt
+    cores = torch.get_num_threads()
+    sample = f"each step: {chains} of the {args.batch} chains x N={args.points} fwd+bwd in float64 torch (autograd backward)"
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "atoms/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic (seeded backbone internal coordinates)",
+        "config": {
+            "workload": "config 1: block reconstruct forward+backward, B=4096 chains, N=768 atoms",
+            "global_batch": args.batch,
+            "points": args.points,
+            "implementation": "the reference path has no CPU code; its algorithm restated in float64 torch (oracle/nerf64.py)",
+        },
+        "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        out = run_reference(args)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return 0
+    dist = Dist(args.gpus)
+    try:
+        out = run_ours(args, dist)
+    finally:
+        torch.cuda.synchronize()
+        dist.close()
+    if dist.rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

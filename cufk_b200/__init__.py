@@ -1,0 +1,17 @@
+"""cufk_b200: B200-native (sm_100a) drop-in for cufk's reconstruction path.
+
+``import cufk_b200 as cufk`` gives the reference's public surface (src/cufk/__init__.py:1-11):
+``reconstruct``, ``compile_torsion``, ``BLOCK_SCAN_MAX_POINT_COUNT`` and ``__version__``.
+"""
+
+from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct
+from .torsion import compile_torsion
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "BLOCK_SCAN_MAX_POINT_COUNT",
+    "__version__",
+    "compile_torsion",
+    "reconstruct",
+]

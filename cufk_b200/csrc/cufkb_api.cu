@@ -1,0 +1,347 @@
+// C ABI of libcufkb.so: validation, launch planning and dispatch of the sm_100a chain kernels.
+//
+// Validation restates the reference's checks (src/cufk/csrc/extension_utils.cuh:119-143):
+// N >= 4, steps = N - 3 <= 2048 (plan_capacity of the float plan, block.cu:88), int32 limits.
+// Differences, by design: B == 0 is a successful no-op (the reference would launch an empty grid
+// and raise), float64 backward is accepted up to 2048 steps (the reference caps it at 1024 by its
+// register plan, block.cu:76-86), and anchors may be NULL for the defaults.
+#include "cufkb.h"
+#include "nerf_kernels.cuh"
+
+#include <atomic>
+#include <cstdint>
+#include <mutex>
+
+namespace {
+
+using cufkb::ChainGeometry;
+
+thread_local int g_last_cuda_error = 0;
+
+constexpr int kMaxDevices = 64;
+constexpr int kTargetItems = 24;       // steps per thread when the batch alone fills the GPU
+constexpr int kMinItems = 5;           // never split a chain below this many steps per thread
+constexpr int kTargetWarpsPerSm = 16;  // resident warps per SM the plan aims for
+
+struct DeviceCache {
+  std::once_flag once;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int error = 0;
+};
+DeviceCache g_devices[kMaxDevices];
+
+// One bit per device: the kernel's dynamic shared-memory limit has been raised there.
+std::atomic<uint64_t> g_attr_done[16];
+
+int current_device(int* dev) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (*dev < 0 || *dev >= kMaxDevices) return static_cast<int>(cudaErrorInvalidDevice);
+  return 0;
+}
+
+const DeviceCache* device_cache(int dev) {
+  DeviceCache& d = g_devices[dev];
+  std::call_once(d.once, [&] {
+    cudaError_t e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    d.error = static_cast<int>(e);
+  });
+  return &d;
+}
+
+int fail_cuda(cudaError_t e) {
+  g_last_cuda_error = static_cast<int>(e);
+  return CUFKB_ERROR_CUDA;
+}
+
+template <typename Kernel>
+cudaError_t ensure_smem_limit(Kernel kernel, int kernel_id, int dev, int max_optin) {
+  const uint64_t bit = uint64_t(1) << dev;
+  if (g_attr_done[kernel_id].load(std::memory_order_acquire) & bit) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin);
+  if (e == cudaSuccess) g_attr_done[kernel_id].fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// Warps per chain and steps per thread.  Long chains get more warps so a thread keeps about
+// kTargetItems steps; small batches get more warps per chain (down to kMinItems steps per thread)
+// so that the grid still offers ~kTargetWarpsPerSm warps per SM.  K is made odd so that the
+// threads' slot strides (3K words) fall on 32 distinct shared-memory banks.
+struct Plan {
+  int threads;
+  int items;
+};
+
+Plan make_plan(int64_t batch, int points, int sm_count) {
+  const int steps = points - 3;
+  int warps = ceil_div(steps, cufkb::kWarp * kTargetItems);
+  if (warps < 1) warps = 1;
+  if (warps > cufkb::kMaxWarps) warps = cufkb::kMaxWarps;
+  const int64_t target = int64_t(sm_count) * kTargetWarpsPerSm;
+  while (warps < cufkb::kMaxWarps && batch * warps < target && ceil_div(steps, cufkb::kWarp * (warps + 1)) >= kMinItems) ++warps;
+  int items = ceil_div(steps, cufkb::kWarp * warps);
+  if ((items & 1) == 0) ++items;
+  return {cufkb::kWarp * warps, items};
+}
+
+size_t elem_size(int dtype) {
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return 4;
+    case CUFKB_FLOAT64:
+      return 8;
+    case CUFKB_FLOAT16:
+    case CUFKB_BFLOAT16:
+      return 2;
+    default:
+      return 0;
+  }
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Shared validation of (dtype, batch, points); returns CUFKB_SUCCESS or an error code.
+int check_shape(int dtype, int64_t batch, int64_t points) {
+  if (elem_size(dtype) == 0) return CUFKB_ERROR_INVALID_DTYPE;
+  if (batch < 0 || batch > INT32_MAX || points > INT32_MAX) return CUFKB_ERROR_SHAPE_LIMITS;
+  if (points < 4) return CUFKB_ERROR_POINT_COUNT;
+  if (points - 3 > CUFKB_MAX_STEPS) return CUFKB_ERROR_TOO_MANY_STEPS;
+  return CUFKB_SUCCESS;
+}
+
+struct LaunchEnv {
+  int dev;
+  const DeviceCache* cache;
+};
+
+int launch_env(LaunchEnv* env) {
+  const int e = current_device(&env->dev);
+  if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
+  env->cache = device_cache(env->dev);
+  if (env->cache->error != 0) return fail_cuda(static_cast<cudaError_t>(env->cache->error));
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz,
+                       int64_t batch, int points, cudaStream_t stream, int kernel_id) {
+  LaunchEnv env;
+  if (int st = launch_env(&env)) return st;
+  const Plan plan = make_plan(batch, points, env.cache->sm_count);
+  const size_t smem = cufkb::block_smem_bytes<T>(points, false);
+  auto kernel = cufkb::block_forward_kernel<T>;
+  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const ChainGeometry geo{points, points - 3, plan.items};
+  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g,
+                        void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
+  LaunchEnv env;
+  if (int st = launch_env(&env)) return st;
+  const Plan plan = make_plan(batch, points, env.cache->sm_count);
+  const size_t smem = cufkb::block_smem_bytes<T>(points, true);
+  auto kernel = cufkb::block_backward_kernel<T>;
+  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const ChainGeometry geo{points, points - 3, plan.items};
+  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                       static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename R>
+cufkb::TorsionConsts<R> torsion_consts(const cufkb_torsion_constants* c) {
+  cufkb::TorsionConsts<R> out;
+  for (int i = 0; i < 3; ++i) {
+    out.length[i] = static_cast<R>(static_cast<float>(c->bond_lengths[i]));
+    out.sin_a[i] = static_cast<R>(c->bond_angle_sin[i]);
+    out.cos_a[i] = static_cast<R>(c->bond_angle_cos[i]);
+  }
+  return out;
+}
+
+template <typename T>
+int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
+                         cudaStream_t stream, int kernel_id) {
+  using R = typename cufkb::ComputeOf<T>::type;
+  LaunchEnv env;
+  if (int st = launch_env(&env)) return st;
+  const Plan plan = make_plan(batch, points, env.cache->sm_count);
+  const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
+  auto kernel = cufkb::torsion_forward_kernel<T>;
+  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  const ChainGeometry geo{points, points - 3, plan.items};
+  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                       static_cast<T*>(xyz), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw,
+                          int64_t grad_stride, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
+  using R = typename cufkb::ComputeOf<T>::type;
+  LaunchEnv env;
+  if (int st = launch_env(&env)) return st;
+  const Plan plan = make_plan(batch, points, env.cache->sm_count);
+  const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
+  auto kernel = cufkb::torsion_backward_kernel<T>;
+  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  const ChainGeometry geo{points, points - 3, plan.items};
+  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                       static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cufkb_max_point_count(void) { return CUFKB_MAX_POINT_COUNT; }
+
+int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                        const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
+                        cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!lengths || !angles || !dihedrals || !xyz) return CUFKB_ERROR_NULL_POINTER;
+  const size_t es = elem_size(dtype);
+  for (const void* p : {lengths, angles, dihedrals, p0, first_direction, initial_normal, static_cast<const void*>(xyz)}) {
+    if (!aligned(p, es)) return CUFKB_ERROR_MISALIGNED;
+  }
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return block_forward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 0);
+    case CUFKB_FLOAT64:
+      return block_forward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 1);
+    case CUFKB_FLOAT16:
+      return block_forward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 2);
+    default:
+      return block_forward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 3);
+  }
+}
+
+int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                         const void* first_direction, const void* initial_normal, const void* grad_xyz, void* grad_lengths,
+                         void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!lengths || !angles || !dihedrals || !grad_xyz || !grad_lengths || !grad_angles || !grad_dihedrals) return CUFKB_ERROR_NULL_POINTER;
+  const size_t es = elem_size(dtype);
+  for (const void* p : {lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, static_cast<const void*>(grad_lengths),
+                        static_cast<const void*>(grad_angles), static_cast<const void*>(grad_dihedrals)}) {
+    if (!aligned(p, es)) return CUFKB_ERROR_MISALIGNED;
+  }
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
+                                        grad_angles, grad_dihedrals, batch, n, s, 4);
+    case CUFKB_FLOAT64:
+      return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
+                                         grad_angles, grad_dihedrals, batch, n, s, 5);
+    case CUFKB_FLOAT16:
+      return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
+                                         grad_angles, grad_dihedrals, batch, n, s, 6);
+    default:
+      return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz,
+                                                grad_lengths, grad_angles, grad_dihedrals, batch, n, s, 7);
+  }
+}
+
+int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                          void* xyz, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!raw_pairs || !xyz) return CUFKB_ERROR_NULL_POINTER;
+  if (!constants) return CUFKB_ERROR_INVALID_VALUE;
+  if (raw_row_stride < 0) return CUFKB_ERROR_BAD_STRIDE;
+  const size_t es = elem_size(dtype);
+  if (!aligned(raw_pairs, es) || !aligned(xyz, es)) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return torsion_forward_impl<float>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 8);
+    case CUFKB_FLOAT64:
+      return torsion_forward_impl<double>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 9);
+    case CUFKB_FLOAT16:
+      return torsion_forward_impl<__half>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 10);
+    default:
+      return torsion_forward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 11);
+  }
+}
+
+int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                           const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
+                           cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!raw_pairs || !grad_xyz || !grad_raw_pairs) return CUFKB_ERROR_NULL_POINTER;
+  if (!constants) return CUFKB_ERROR_INVALID_VALUE;
+  if (raw_row_stride < 0 || grad_row_stride < 0 || (batch > 1 && grad_row_stride < 2 * (points - 3))) return CUFKB_ERROR_BAD_STRIDE;
+  const size_t es = elem_size(dtype);
+  if (!aligned(raw_pairs, es) || !aligned(grad_xyz, es) || !aligned(grad_raw_pairs, es)) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return torsion_backward_impl<float>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s, 12);
+    case CUFKB_FLOAT64:
+      return torsion_backward_impl<double>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s,
+                                           13);
+    case CUFKB_FLOAT16:
+      return torsion_backward_impl<__half>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s,
+                                           14);
+    default:
+      return torsion_backward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch,
+                                                  n, s, 15);
+  }
+}
+
+const char* cufkb_status_string(int status) {
+  switch (status) {
+    case CUFKB_SUCCESS:
+      return "success";
+    case CUFKB_ERROR_INVALID_DTYPE:
+      return "dtype must be float32, float64, float16, or bfloat16";
+    case CUFKB_ERROR_NULL_POINTER:
+      return "a required buffer is NULL";
+    case CUFKB_ERROR_POINT_COUNT:
+      return "point_count must be >= 4";
+    case CUFKB_ERROR_TOO_MANY_STEPS:
+      return "supports at most 2048 local transforms";
+    case CUFKB_ERROR_SHAPE_LIMITS:
+      return "shape exceeds int32 kernel limits";
+    case CUFKB_ERROR_BAD_STRIDE:
+      return "row stride too small for the pairs of one chain";
+    case CUFKB_ERROR_MISALIGNED:
+      return "pointer not aligned to its element size";
+    case CUFKB_ERROR_INVALID_VALUE:
+      return "torsion constants must not be NULL";
+    case CUFKB_ERROR_CUDA:
+      return "CUDA runtime error";
+    default:
+      return "unknown status";
+  }
+}
+
+int cufkb_last_cuda_error(void) { return g_last_cuda_error; }
+
+}  // extern "C"

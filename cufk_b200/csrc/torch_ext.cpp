@@ -1,0 +1,313 @@
+// PyTorch boundary of cufk_b200: the C++ autograd `apply` wrappers around the C ABI (cufkb.h).
+//
+// Mirrors the reference's extension (src/cufk/csrc/block.cu:367-445, torsion.cu:413-447) and its
+// checks (src/cufk/csrc/extension_utils.cuh:57-143): same argument meaning, same error texts, outputs
+// allocated through the caching allocator on the input's device, launches on the current stream
+// under a device guard, no host synchronisation.  Anchors may be None (the kernel then uses the
+// defaults without any host-to-device copy).  This file holds host code only; every kernel lives in
+// libcufkb.so.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/autograd.h>
+#include <torch/extension.h>
+
+#include <optional>
+#include <vector>
+
+#include "cufkb.h"
+
+namespace {
+
+using torch::Tensor;
+using torch::autograd::AutogradContext;
+using torch::autograd::tensor_list;
+
+constexpr int kMaxSteps = CUFKB_MAX_STEPS;
+
+bool supported_dtype(torch::ScalarType t) {
+  return t == torch::kFloat32 || t == torch::kFloat64 || t == torch::kFloat16 || t == torch::kBFloat16;
+}
+
+int dtype_code(torch::ScalarType t) {
+  switch (t) {
+    case torch::kFloat32:
+      return CUFKB_FLOAT32;
+    case torch::kFloat64:
+      return CUFKB_FLOAT64;
+    case torch::kFloat16:
+      return CUFKB_FLOAT16;
+    case torch::kBFloat16:
+      return CUFKB_BFLOAT16;
+    default:
+      TORCH_CHECK(false, "unsupported dtype");
+  }
+}
+
+// extension_utils.cuh:57-61
+void check_cuda_float(const Tensor& x, const char* name) {
+  TORCH_CHECK(x.is_cuda(), name, " must be CUDA");
+  TORCH_CHECK(supported_dtype(x.scalar_type()), name, " must be float32, float64, float16, or bfloat16");
+  TORCH_CHECK(x.is_contiguous(), name, " must be contiguous");
+}
+
+// extension_utils.cuh:63-68
+void check_cuda_float_row_contiguous(const Tensor& x, const char* name) {
+  TORCH_CHECK(x.is_cuda(), name, " must be CUDA");
+  TORCH_CHECK(supported_dtype(x.scalar_type()), name, " must be float32, float64, float16, or bfloat16");
+  TORCH_CHECK(x.dim() == 2, name, " must have shape (B, K)");
+  TORCH_CHECK(x.stride(1) == 1, name, " must have stride(1) == 1");
+}
+
+// extension_utils.cuh:70-74
+void check_like(const Tensor& x, const Tensor& ref, const char* name) {
+  check_cuda_float(x, name);
+  TORCH_CHECK(x.scalar_type() == ref.scalar_type(), name, " must have the same dtype as reference");
+  TORCH_CHECK(x.device() == ref.device(), name, " must be on the same device as reference");
+}
+
+// extension_utils.cuh:76-82; an undefined tensor means "use the default anchor"
+Tensor checked_anchor(const Tensor& x, const Tensor& ref, const char* name) {
+  if (!x.defined()) return x;
+  TORCH_CHECK(x.is_cuda(), name, " must be CUDA");
+  TORCH_CHECK(x.scalar_type() == ref.scalar_type(), name, " must have the same dtype as reference");
+  TORCH_CHECK(x.device() == ref.device(), name, " must be on the same device as reference");
+  TORCH_CHECK(x.sizes() == torch::IntArrayRef({3}), name, " must have shape (3,)");
+  TORCH_CHECK(!x.requires_grad(), name, " gradients are not supported");
+  return x.contiguous();
+}
+
+struct Shape {
+  int64_t batch;
+  int64_t points;
+};
+
+// extension_utils.cuh:119-126
+Shape chain_shape_from_steps(const Tensor& ref, int64_t steps) {
+  TORCH_CHECK(ref.size(0) <= INT32_MAX && steps + 3 <= INT32_MAX, "shape exceeds int32 kernel limits");
+  TORCH_CHECK(steps >= 1, "point_count must be >= 4");
+  return {ref.size(0), steps + 3};
+}
+
+// the step cap of ChainLaunch (extension_utils.cuh:128-143), checked after the anchors
+void check_max_local_transforms(const Shape& shape, const char* op_name) {
+  TORCH_CHECK(shape.points - 3 <= kMaxSteps, op_name, " supports at most ", kMaxSteps, " local transforms");
+}
+
+// block.cu:367-378
+Shape check_geom(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals) {
+  check_cuda_float(lengths, "lengths");
+  check_like(angles, lengths, "angles");
+  check_like(dihedrals, lengths, "dihedrals");
+  TORCH_CHECK(lengths.dim() == 2, "lengths must have shape (B, N-1)");
+  TORCH_CHECK(angles.dim() == 2, "angles must have shape (B, N-2)");
+  TORCH_CHECK(dihedrals.dim() == 2, "dihedrals must have shape (B, N-3)");
+  const Shape shape = chain_shape_from_steps(lengths, lengths.size(1) - 2);
+  TORCH_CHECK(angles.sizes() == torch::IntArrayRef({shape.batch, shape.points - 2}), "bad angles shape");
+  TORCH_CHECK(dihedrals.sizes() == torch::IntArrayRef({shape.batch, shape.points - 3}), "bad dihedrals shape");
+  return shape;
+}
+
+// torsion.cu:413-417
+Shape check_pairs(const Tensor& raw) {
+  check_cuda_float_row_contiguous(raw, "raw_pairs");
+  TORCH_CHECK(raw.size(1) % 2 == 0, "raw_pairs second dimension must be even");
+  const Shape shape = chain_shape_from_steps(raw, raw.size(1) / 2);
+  check_max_local_transforms(shape, "torsion_pairs");
+  return shape;
+}
+
+void check_status(int status, const char* op) {
+  if (status == CUFKB_SUCCESS) return;
+  if (status == CUFKB_ERROR_CUDA) {
+    const auto err = static_cast<cudaError_t>(cufkb_last_cuda_error());
+    TORCH_CHECK(false, op, ": CUDA error: ", cudaGetErrorString(err));
+  }
+  TORCH_CHECK(false, op, ": ", cufkb_status_string(status));
+}
+
+const void* ptr_or_null(const Tensor& t) { return t.defined() ? t.data_ptr() : nullptr; }
+
+cufkb_stream_t current_stream() { return reinterpret_cast<cufkb_stream_t>(at::cuda::getCurrentCUDAStream().stream()); }
+
+struct Anchors {
+  Tensor p0, first_direction, initial_normal;
+};
+
+Anchors checked_anchors(const Tensor& p0, const Tensor& fd, const Tensor& nn, const Tensor& ref, const Shape& shape) {
+  Anchors a{checked_anchor(p0, ref, "p0"), checked_anchor(fd, ref, "first_direction"), checked_anchor(nn, ref, "initial_normal")};
+  check_max_local_transforms(shape, "reconstruct");
+  return a;
+}
+
+Tensor block_forward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor xyz = torch::empty({shape.batch, shape.points, 3}, lengths.options());
+  check_status(cufkb_block_forward(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                   ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
+                                   shape.batch, shape.points, current_stream()),
+               "reconstruct");
+  return xyz;
+}
+
+std::vector<Tensor> block_backward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a,
+                                        const Tensor& grad_points, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor gl = torch::empty_like(lengths);
+  Tensor ga = torch::empty_like(angles);
+  Tensor gd = torch::empty_like(dihedrals);
+  check_status(cufkb_block_backward(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                    ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                    grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(), shape.batch, shape.points,
+                                    current_stream()),
+               "reconstruct backward");
+  return {gl, ga, gd};
+}
+
+Tensor opt(const std::optional<Tensor>& t) { return t.has_value() ? *t : Tensor(); }
+
+// block.cu:393-429
+class ReconstructAutograd : public torch::autograd::Function<ReconstructAutograd> {
+ public:
+  // Anchors are optional non-variable arguments: torch's autograd Function records every Tensor
+  // argument as a differentiable input and cannot take an undefined one.
+  static Tensor forward(AutogradContext* ctx, Tensor lengths, Tensor angles, Tensor dihedrals, std::optional<Tensor> p0,
+                        std::optional<Tensor> first_direction, std::optional<Tensor> initial_normal) {
+    const Shape shape = check_geom(lengths, angles, dihedrals);
+    const Anchors a = checked_anchors(opt(p0), opt(first_direction), opt(initial_normal), lengths, shape);
+    Tensor xyz = block_forward_impl(lengths, angles, dihedrals, a, shape);
+    ctx->save_for_backward({lengths, angles, dihedrals});
+    ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
+    ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
+    ctx->saved_data["initial_normal"] = a.initial_normal.defined() ? c10::IValue(a.initial_normal) : c10::IValue();
+    return xyz;
+  }
+
+  static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+    const auto saved = ctx->get_saved_variables();
+    const Tensor& lengths = saved[0];
+    const Tensor& angles = saved[1];
+    const Tensor& dihedrals = saved[2];
+    Tensor grad_points = grad_outputs[0].is_contiguous() ? grad_outputs[0] : grad_outputs[0].contiguous();
+    check_like(grad_points, lengths, "grad_points");
+    const Shape shape = check_geom(lengths, angles, dihedrals);
+    auto anchor = [&](const char* key) {
+      const c10::IValue& v = ctx->saved_data[key];
+      return v.isTensor() ? v.toTensor() : Tensor();
+    };
+    const Anchors a{anchor("p0"), anchor("first_direction"), anchor("initial_normal")};
+    auto grads = block_backward_impl(lengths, angles, dihedrals, a, grad_points, shape);
+    return {grads[0], grads[1], grads[2], Tensor(), Tensor(), Tensor()};
+  }
+};
+
+Tensor apply_autograd(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                      const std::optional<Tensor>& first_direction, const std::optional<Tensor>& initial_normal) {
+  return ReconstructAutograd::apply(lengths, angles, dihedrals, p0, first_direction, initial_normal);
+}
+
+// ---------------------------------------------------------------------------------------------
+// torsion path: constants are a run-time argument (9 doubles), not a JIT build
+// ---------------------------------------------------------------------------------------------
+cufkb_torsion_constants torsion_constants(const std::vector<double>& c) {
+  TORCH_CHECK(c.size() == 9, "torsion constants must be 3 bond lengths, 3 angle sines and 3 angle cosines");
+  cufkb_torsion_constants out;
+  for (int i = 0; i < 3; ++i) {
+    out.bond_lengths[i] = c[i];
+    out.bond_angle_sin[i] = c[3 + i];
+    out.bond_angle_cos[i] = c[6 + i];
+  }
+  return out;
+}
+
+Tensor torsion_forward_impl(const Tensor& raw, const std::vector<double>& consts, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(raw.device());
+  const cufkb_torsion_constants c = torsion_constants(consts);
+  Tensor xyz = torch::empty({shape.batch, shape.points, 3}, raw.options());
+  check_status(cufkb_torsion_forward(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr(), shape.batch,
+                                     shape.points, current_stream()),
+               "torsion_pairs");
+  return xyz;
+}
+
+Tensor torsion_backward_impl(const Tensor& raw, const std::vector<double>& consts, const Tensor& grad_points, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(raw.device());
+  const cufkb_torsion_constants c = torsion_constants(consts);
+  // the reference copies raw's strides (empty_strided_like, extension_utils.cuh:162-164); rows that
+  // would overlap (a broadcast row stride) get a contiguous gradient instead
+  Tensor grad = (shape.batch <= 1 || raw.stride(0) >= raw.size(1)) ? torch::empty_strided(raw.sizes(), raw.strides(), raw.options())
+                                                                    : torch::empty(raw.sizes(), raw.options());
+  check_status(cufkb_torsion_backward(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, grad_points.data_ptr(),
+                                      grad.data_ptr(), grad.stride(0), shape.batch, shape.points, current_stream()),
+               "torsion_pairs backward");
+  return grad;
+}
+
+// torsion.cu:419-437; the forward saves only raw_pairs (the backward recomputes the chain)
+class TorsionAutograd : public torch::autograd::Function<TorsionAutograd> {
+ public:
+  static Tensor forward(AutogradContext* ctx, Tensor raw_pairs, std::vector<double> consts) {
+    const Shape shape = check_pairs(raw_pairs);
+    Tensor xyz = torsion_forward_impl(raw_pairs, consts, shape);
+    ctx->save_for_backward({raw_pairs});
+    ctx->saved_data["consts"] = c10::IValue(consts);
+    return xyz;
+  }
+
+  static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+    const auto saved = ctx->get_saved_variables();
+    const Tensor& raw = saved[0];
+    const std::vector<double> consts = ctx->saved_data["consts"].toDoubleVector();
+    Tensor grad_points = grad_outputs[0].is_contiguous() ? grad_outputs[0] : grad_outputs[0].contiguous();
+    check_like(grad_points, raw, "grad_points");
+    const Shape shape = check_pairs(raw);
+    return {torsion_backward_impl(raw, consts, grad_points, shape), Tensor()};
+  }
+};
+
+Tensor torsion_apply(const Tensor& raw_pairs, const std::vector<double>& consts) { return TorsionAutograd::apply(raw_pairs, consts); }
+
+// ---------------------------------------------------------------------------------------------
+// autograd-free entry points (benchmarks, CUDA-graph capture); same checks and kernels
+// ---------------------------------------------------------------------------------------------
+Tensor block_forward(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                     const std::optional<Tensor>& fd, const std::optional<Tensor>& nn) {
+  const Shape shape = check_geom(lengths, angles, dihedrals);
+  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
+  return block_forward_impl(lengths, angles, dihedrals, a, shape);
+}
+
+std::vector<Tensor> block_backward(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                                   const std::optional<Tensor>& fd, const std::optional<Tensor>& nn, const Tensor& grad_points) {
+  const Shape shape = check_geom(lengths, angles, dihedrals);
+  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
+  check_like(grad_points, lengths, "grad_points");
+  TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
+  return block_backward_impl(lengths, angles, dihedrals, a, grad_points, shape);
+}
+
+Tensor torsion_forward(const Tensor& raw, const std::vector<double>& consts) { return torsion_forward_impl(raw, consts, check_pairs(raw)); }
+
+Tensor torsion_backward(const Tensor& raw, const std::vector<double>& consts, const Tensor& grad_points) {
+  const Shape shape = check_pairs(raw);
+  check_like(grad_points, raw, "grad_points");
+  TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
+  return torsion_backward_impl(raw, consts, grad_points, shape);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("apply", &apply_autograd, "reconstruct autograd apply", pybind11::arg("lengths"), pybind11::arg("angles"),
+        pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
+        pybind11::arg("initial_normal") = pybind11::none());
+  m.def("torsion_apply", &torsion_apply, "torsion-only autograd apply", pybind11::arg("raw_pairs"), pybind11::arg("constants"));
+  m.def("block_forward", &block_forward, "forward kernel only", pybind11::arg("lengths"), pybind11::arg("angles"),
+        pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
+        pybind11::arg("initial_normal") = pybind11::none());
+  m.def("block_backward", &block_backward, "backward kernel only", pybind11::arg("lengths"), pybind11::arg("angles"),
+        pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
+        pybind11::arg("grad_points"));
+  m.def("torsion_forward", &torsion_forward, "torsion forward kernel only");
+  m.def("torsion_backward", &torsion_backward, "torsion backward kernel only");
+  m.def("max_point_count", &cufkb_max_point_count);
+}

@@ -1,0 +1,57 @@
+"""``reconstruct``: the drop-in for ``cufk.reconstruct`` (src/cufk/reconstruct.py:29-81).
+
+Same signature, shapes, dtypes, defaults and error behaviour.  The work runs in the sm_100a
+kernels of ``libcufkb.so`` through the C++ autograd wrapper ``_C.apply``.  Omitted anchors are
+passed as ``None``; the kernels then use the reference defaults directly instead of building three
+small device tensors per call (reconstruct.py:19-26, 69-71).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._native import _C
+
+BLOCK_SCAN_MAX_POINT_COUNT = 2051
+
+
+def _batched_inputs(
+    lengths: torch.Tensor,
+    angles: torch.Tensor,
+    dihedrals: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, bool]:
+    single = lengths.dim() == 1
+    if single:
+        lengths, angles, dihedrals = lengths[None], angles[None], dihedrals[None]
+    return lengths, angles, dihedrals, single
+
+
+def reconstruct(
+    lengths: torch.Tensor,
+    angles: torch.Tensor,
+    dihedrals: torch.Tensor,
+    p0: torch.Tensor | None = None,
+    first_direction: torch.Tensor | None = None,
+    initial_normal: torch.Tensor | None = None,
+) -> torch.Tensor:
+    r"""Reconstruct Cartesian coordinates from full internal coordinates.
+
+    Args:
+        lengths: Bond lengths. CUDA tensor shaped ``(N - 1,)`` for one chain or ``(B, N - 1)``.
+        angles: Bond angles in radians, ``(N - 2,)`` or ``(B, N - 2)``.
+        dihedrals: Dihedral angles in radians, ``(N - 3,)`` or ``(B, N - 3)``.
+        p0: Optional first point, shaped ``(3,)``; default ``(0, 0, 0)``.
+        first_direction: Optional first-bond direction, ``(3,)``; default ``(1, 0, 0)``.
+        initial_normal: Optional initial plane normal, ``(3,)``; default ``(0, 0, 1)``.
+
+    Returns:
+        ``(N, 3)`` for one chain or ``(B, N, 3)``, with the dtype of ``lengths``.
+
+    Notes:
+        Inputs are CUDA tensors of one dtype among float16, bfloat16, float32 and float64, with
+        4 <= N <= 2051.  Gradients flow to lengths, angles and dihedrals; anchors take none.
+        16-bit inputs are computed in float32 and rounded once on output.
+    """
+    lengths, angles, dihedrals, single = _batched_inputs(lengths, angles, dihedrals)
+    xyz = _C.apply(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
+    return xyz[0] if single else xyz

@@ -1,0 +1,107 @@
+/*
+ * cufkb.h — C ABI of the B200 (sm_100a) NeRF chain-reconstruction library (libcufkb.so).
+ *
+ * Drop-in boundary for the reconstruction hot path of cufk (xsjk/cufk).  Each entry point takes
+ * plain device pointers, sizes, a dtype code and a CUDA stream, launches asynchronously on that
+ * stream and returns a status code; it never allocates, never synchronises and keeps no state
+ * besides a per-device cache of the SM count and kernel attributes.  Inputs are read-only.
+ *
+ * Shapes (all row-major, contiguous rows):
+ *   lengths (B, N-1), angles (B, N-2), dihedrals (B, N-3), xyz / grad_xyz (B, N, 3);
+ *   raw_pairs (B, 2(N-3)) interleaved [sin_0, cos_0, sin_1, cos_1, ...] with any row stride;
+ *   anchors p0 / first_direction / initial_normal: 3 elements each, or NULL for the reference's
+ *   defaults (0,0,0), (1,0,0), (0,0,1).
+ * Limits: 4 <= N <= CUFKB_MAX_POINT_COUNT (2051), 0 <= B <= INT32_MAX; B == 0 launches nothing.
+ * Every pointer must be aligned to its element size.  All floating-point arithmetic of the 16-bit
+ * types is done in float (rounded once on output); float64 computes in double.
+ *
+ * Reference interfaces replaced (paths relative to the cufk project root):
+ *   cufkb_block_forward   <- forward_cuda_impl<T>   src/cufk/csrc/block.cu:319-329
+ *                            (reached from _C.apply, block.cu:431-445 / _C.pyi:3-10)
+ *   cufkb_block_backward  <- backward_cuda_impl<T>  src/cufk/csrc/block.cu:331-365
+ *   cufkb_torsion_forward <- forward_default_impl<T> src/cufk/csrc/torsion.cu:387-397
+ *   cufkb_torsion_backward<- backward_xyz_impl<T>   src/cufk/csrc/torsion.cu:399-411
+ *   validation codes      <- TORCH_CHECKs of src/cufk/csrc/extension_utils.cuh:57-143
+ */
+#ifndef CUFKB_H_
+#define CUFKB_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* cufkb_stream_t;
+
+#define CUFKB_MAX_POINT_COUNT 2051
+#define CUFKB_MAX_STEPS 2048
+
+/* Storage dtype of every floating-point buffer of one call. */
+enum cufkb_dtype {
+  CUFKB_FLOAT32 = 0,
+  CUFKB_FLOAT64 = 1,
+  CUFKB_FLOAT16 = 2,
+  CUFKB_BFLOAT16 = 3
+};
+
+enum cufkb_status {
+  CUFKB_SUCCESS = 0,
+  CUFKB_ERROR_INVALID_DTYPE = 1,  /* "must be float32, float64, float16, or bfloat16" */
+  CUFKB_ERROR_NULL_POINTER = 2,   /* a required buffer is NULL while B > 0 */
+  CUFKB_ERROR_POINT_COUNT = 3,    /* "point_count must be >= 4" */
+  CUFKB_ERROR_TOO_MANY_STEPS = 4, /* "supports at most 2048 local transforms" */
+  CUFKB_ERROR_SHAPE_LIMITS = 5,   /* "shape exceeds int32 kernel limits" (or B < 0) */
+  CUFKB_ERROR_BAD_STRIDE = 6,     /* torsion row stride too small for the pairs */
+  CUFKB_ERROR_MISALIGNED = 7,     /* a pointer not aligned to its element size */
+  CUFKB_ERROR_INVALID_VALUE = 8,  /* NULL torsion constants */
+  CUFKB_ERROR_CUDA = 9            /* a CUDA runtime error; see cufkb_last_cuda_error() */
+};
+
+/* Backbone constants of compile_torsion(bond_lengths, bond_angles).  Bond i is used by every
+ * step whose length phase is i; lengths are rounded to float32 inside the library, as the
+ * reference compiles them (src/cufk/csrc/torsion.cu:43-47); the angle sine/cosine are given in
+ * double, as src/cufk/torsion.py:81-86 computes them on the host. */
+typedef struct cufkb_torsion_constants {
+  double bond_lengths[3];
+  double bond_angle_sin[3];
+  double bond_angle_cos[3];
+} cufkb_torsion_constants;
+
+/* 2051 = BLOCK_SCAN_MAX_POINT_COUNT (src/cufk/reconstruct.py:5). */
+int cufkb_max_point_count(void);
+
+/* xyz (B, N, 3) from lengths/angles/dihedrals and the three optional anchors. */
+int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                        const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
+                        cufkb_stream_t stream);
+
+/* Gradients of sum(grad_xyz * xyz) w.r.t. lengths, angles and dihedrals (no anchor gradients).
+ * Recomputes the forward prefix; needs nothing saved from cufkb_block_forward. */
+int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                         const void* first_direction, const void* initial_normal, const void* grad_xyz, void* grad_lengths,
+                         void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream);
+
+/* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
+ * elements (any stride >= 0, pairs within a row contiguous). */
+int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                          void* xyz, int64_t batch, int64_t points, cufkb_stream_t stream);
+
+/* Gradient w.r.t. the raw pairs; grad row b starts at grad_raw_pairs + b * grad_row_stride
+ * (stride >= 2(N-3) when B > 1).  Recomputes the forward; reads no saved xyz. */
+int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                           const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
+                           cufkb_stream_t stream);
+
+/* Static text for a status code. */
+const char* cufkb_status_string(int status);
+
+/* cudaError_t value of the last CUFKB_ERROR_CUDA returned on the calling thread (0 if none). */
+int cufkb_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUFKB_H_ */

@@ -1,0 +1,79 @@
+"""CPU checks of the Python surface: names, caching, error text for host tensors, and that the
+product never imports the oracle (the checker) or falls back to a CPU path."""
+
+from __future__ import annotations
+
+import ast
+from pathlib import Path
+
+import pytest
+import torch
+
+import cufk_b200 as cufk
+
+PKG = Path(cufk.__file__).resolve().parent
+
+
+def test_public_surface_matches_reference():
+    assert set(cufk.__all__) == {"BLOCK_SCAN_MAX_POINT_COUNT", "__version__", "compile_torsion", "reconstruct"}
+    assert cufk.BLOCK_SCAN_MAX_POINT_COUNT == 2051
+    assert cufk.__version__ == "0.1.0"
+
+
+def test_host_tensors_are_rejected_with_reference_text():
+    with pytest.raises(RuntimeError, match="lengths must be CUDA"):
+        cufk.reconstruct(torch.ones(2, 9), torch.ones(2, 8), torch.ones(2, 7))
+    with pytest.raises(RuntimeError, match="lengths must be CUDA"):
+        cufk.reconstruct(torch.ones(9), torch.ones(8), torch.ones(7))
+    with pytest.raises(RuntimeError, match="raw_pairs must be CUDA"):
+        cufk.compile_torsion((1.0, 1.0, 1.0), (2.0, 2.0, 2.0))(torch.ones(2, 8))
+
+
+def test_compile_torsion_is_cached_per_constants():
+    a = cufk.compile_torsion((0.1, 0.2, 0.3), (1.0, 2.0, 3.0))
+    b = cufk.compile_torsion((0.1, 0.2, 0.3), (1.0, 2.0, 3.0))
+    c = cufk.compile_torsion((0.1, 0.2, 0.3), (1.0, 2.0, 3.5))
+    assert a is b and a is not c
+    with pytest.raises(AssertionError, match="bond_angles must have 3 elements"):
+        cufk.compile_torsion((0.1, 0.2, 0.3), (1.0, 2.0))
+
+
+def test_product_never_imports_the_oracle():
+    for path in PKG.rglob("*.py"):
+        tree = ast.parse(path.read_text())
+        for node in ast.walk(tree):
+            if isinstance(node, ast.Import):
+                names = [a.name for a in node.names]
+            elif isinstance(node, ast.ImportFrom):
+                names = [node.module or ""]
+            else:
+                continue
+            assert not any(n.split(".")[0] in ("oracle", "tests", "_work") for n in names), (path, names)
+
+
+def test_native_extension_is_loaded():
+    from cufk_b200 import _native
+
+    assert _native.LIB_PATH.exists()
+    assert hasattr(_native._C, "apply") and hasattr(_native._C, "torsion_apply")
+
+
+def test_bench_and_oracle_generate_the_same_inputs():
+    import bench
+    from oracle import nerf64
+
+    a = bench.make_inputs(5, 40, seed=3)
+    b = nerf64.make_inputs(5, 40, seed=3)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+
+
+def test_shards_cover_the_batch():
+    import bench
+
+    for world in (1, 2, 3, 4, 8):
+        ranges = [bench.shard(4096, world, r) for r in range(world)]
+        assert ranges[0][0] == 0 and ranges[-1][1] == 4096
+        assert all(ranges[i][1] == ranges[i + 1][0] for i in range(world - 1))
+        sizes = [hi - lo for lo, hi in ranges]
+        assert max(sizes) - min(sizes) <= 1

@@ -1,0 +1,107 @@
+"""CPU checks of the C ABI (include/cufkb.h, cufk_b200/libcufkb.so): loading, exported symbols and
+argument validation.  Validation returns before any CUDA call, so no GPU is needed; the fake
+pointers passed here are never dereferenced."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "cufkb.h"
+LIB = ROOT / "cufk_b200" / "libcufkb.so"
+
+SUCCESS, INVALID_DTYPE, NULL_POINTER, POINT_COUNT, TOO_MANY_STEPS, SHAPE_LIMITS, BAD_STRIDE, MISALIGNED, INVALID_VALUE, CUDA = range(10)
+F32, F64, F16, BF16 = range(4)
+
+
+class TorsionConstants(ctypes.Structure):
+    _fields_ = [("bond_lengths", ctypes.c_double * 3), ("bond_angle_sin", ctypes.c_double * 3), ("bond_angle_cos", ctypes.c_double * 3)]
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(cufkb_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    lib = ctypes.CDLL(str(LIB))
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_backward.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_torsion_forward.argtypes = [ctypes.c_int, vp, i64, ctypes.POINTER(TorsionConstants), vp, i64, i64, vp]
+    lib.cufkb_torsion_backward.argtypes = [ctypes.c_int, vp, i64, ctypes.POINTER(TorsionConstants), vp, vp, i64, i64, i64, vp]
+    lib.cufkb_status_string.restype = ctypes.c_char_p
+    return lib
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    assert {"cufkb_block_forward", "cufkb_block_backward", "cufkb_torsion_forward", "cufkb_torsion_backward"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_max_point_count(lib):
+    assert lib.cufkb_max_point_count() == 2051
+
+
+def fwd(lib, dtype=F32, L=16, A=32, D=48, xyz=64, batch=2, points=10, anchors=(None, None, None)):
+    return lib.cufkb_block_forward(dtype, L, A, D, *anchors, xyz, batch, points, None)
+
+
+def test_block_forward_validation(lib):
+    assert fwd(lib, dtype=9) == INVALID_DTYPE
+    assert fwd(lib, points=3) == POINT_COUNT
+    assert fwd(lib, points=2052) == TOO_MANY_STEPS
+    assert fwd(lib, batch=-1) == SHAPE_LIMITS
+    assert fwd(lib, batch=2**31) == SHAPE_LIMITS
+    assert fwd(lib, points=2**31 + 5) == SHAPE_LIMITS
+    assert fwd(lib, batch=0, L=None, A=None, D=None, xyz=None) == SUCCESS
+    assert fwd(lib, L=None) == NULL_POINTER
+    assert fwd(lib, xyz=None) == NULL_POINTER
+    assert fwd(lib, L=18) == MISALIGNED
+    assert fwd(lib, dtype=F64, L=20) == MISALIGNED
+    assert fwd(lib, anchors=(17, None, None)) == MISALIGNED
+
+
+def test_block_backward_validation(lib):
+    def bwd(**kw):
+        args = dict(dtype=F32, L=16, A=32, D=48, g=64, gl=80, ga=96, gd=112, batch=2, points=10)
+        args.update(kw)
+        return lib.cufkb_block_backward(
+            args["dtype"], args["L"], args["A"], args["D"], None, None, None, args["g"], args["gl"], args["ga"], args["gd"],
+            args["batch"], args["points"], None,
+        )
+
+    assert bwd(points=3) == POINT_COUNT
+    assert bwd(points=2051 + 1) == TOO_MANY_STEPS
+    assert bwd(batch=0, L=None, g=None) == SUCCESS
+    assert bwd(g=None) == NULL_POINTER
+    assert bwd(gd=None) == NULL_POINTER
+    assert bwd(gl=82) == MISALIGNED
+
+
+def test_torsion_validation(lib):
+    c = TorsionConstants()
+    assert lib.cufkb_torsion_forward(F32, 16, -1, ctypes.byref(c), 64, 2, 10, None) == BAD_STRIDE
+    assert lib.cufkb_torsion_forward(F32, 16, 14, None, 64, 2, 10, None) == INVALID_VALUE
+    assert lib.cufkb_torsion_forward(F32, 16, 14, ctypes.byref(c), 64, 2, 3, None) == POINT_COUNT
+    assert lib.cufkb_torsion_backward(F32, 16, 14, ctypes.byref(c), 64, 128, 13, 2, 10, None) == BAD_STRIDE
+    assert lib.cufkb_torsion_backward(F32, 16, 14, ctypes.byref(c), 64, None, 14, 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_torsion_backward(F32, 16, 14, ctypes.byref(c), 64, 128, 14, 0, 10, None) == SUCCESS
+
+
+def test_status_strings(lib):
+    assert lib.cufkb_status_string(SUCCESS) == b"success"
+    assert lib.cufkb_status_string(POINT_COUNT) == b"point_count must be >= 4"
+    assert b"2048 local transforms" in lib.cufkb_status_string(TOO_MANY_STEPS)
+    assert lib.cufkb_status_string(12345) == b"unknown status"
+    assert lib.cufkb_last_cuda_error() == 0

@@ -1,0 +1,111 @@
+"""Parity against the reference's own kernels, compiled for sm_100a into oracle/_ref/.
+
+Skipped when ``oracle/build_ref.py`` has not been run.  Checks that (1) the reference kernels and the
+float64 oracle agree (pinning the oracle), (2) cufk_b200 and the reference agree within the fp32
+tolerance, and (3) for 16-bit storage cufk_b200's error against float64 is no worse than the
+reference's own low-precision path (which computes its payload in the 16-bit type).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import cufk_b200 as cufk
+from oracle import nerf64, ref_kernels
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not ref_kernels.available("block"), reason="reference kernels not built")]
+
+F64 = torch.float64
+ANCHOR_KEYS = ("p0", "first_direction", "initial_normal")
+
+
+def grads_of(fn, inp, dtype, anchors):
+    L = inp["lengths"].to("cuda", dtype).requires_grad_(True)
+    A = inp["angles"].to("cuda", dtype).requires_grad_(True)
+    D = inp["dihedrals"].to("cuda", dtype).requires_grad_(True)
+    kw = {k: inp[k].to("cuda", dtype) for k in ANCHOR_KEYS} if anchors else {}
+    xyz = fn(L, A, D, **kw)
+    xyz.backward(inp["grad"].to("cuda", dtype))
+    return [t.detach().double().cpu() for t in (xyz, L.grad, A.grad, D.grad)]
+
+
+def errors(got, ref):
+    xerr = float((got[0] - ref[0]).abs().max())
+    gerr = max(float((a - b).norm() / b.norm()) for a, b in zip(got[1:], ref[1:]))
+    return xerr, gerr
+
+
+@pytest.mark.parametrize("points,anchors", [(4, False), (384, False), (768, True), (1026, False), (2051, True)])
+def test_fp32_three_way(points, anchors):
+    inp = nerf64.make_inputs(8, points, seed=points, anchors=anchors)
+    cast = {k: v.double() for k, v in inp.items()}
+    kw = {k: cast[k] for k in ANCHOR_KEYS} if anchors else {}
+    oracle = list(nerf64.reconstruct64_with_grads(cast["lengths"], cast["angles"], cast["dihedrals"], cast["grad"], **kw))
+    ref = grads_of(ref_kernels.ref_reconstruct, inp, torch.float32, anchors)
+    ours = grads_of(cufk.reconstruct, inp, torch.float32, anchors)
+    rx, rg = errors(ref, oracle)
+    ox, og = errors(ours, oracle)
+    assert rx <= 5e-4 and rg <= 1e-4, (rx, rg)  # the oracle is pinned by the reference
+    assert ox <= 5e-4 and og <= 1e-4, (ox, og)
+    dx, dg = errors(ours, ref)
+    assert dx <= 5e-4 and dg <= 1e-4, (dx, dg)
+
+
+@pytest.mark.parametrize("points", [4, 257, 1027])
+def test_fp64_three_way(points):
+    inp = nerf64.make_inputs(4, points, seed=points, dtype=F64, anchors=True)
+    oracle = list(nerf64.reconstruct64_with_grads(inp["lengths"], inp["angles"], inp["dihedrals"], inp["grad"], **{k: inp[k] for k in ANCHOR_KEYS}))
+    ref = grads_of(ref_kernels.ref_reconstruct, inp, F64, True)
+    ours = grads_of(cufk.reconstruct, inp, F64, True)
+    assert max(errors(ref, oracle)) <= 1e-9
+    assert max(errors(ours, oracle)) <= 1e-9
+
+
+def test_fp64_backward_beyond_reference_cap():
+    # the reference refuses float64 backward above 1024 steps; cufk_b200 accepts it
+    inp = nerf64.make_inputs(1, 2051, seed=1, dtype=F64)
+    with pytest.raises(RuntimeError, match="backward supports at most"):
+        grads_of(ref_kernels.ref_reconstruct, inp, F64, False)
+    ours = grads_of(cufk.reconstruct, inp, F64, False)
+    oracle = nerf64.reconstruct64_with_grads(inp["lengths"], inp["angles"], inp["dihedrals"], inp["grad"])
+    assert max(errors(ours, list(oracle))) <= 1e-9
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("points", [384, 1026])
+def test_low_precision_no_worse_than_reference(dtype, points):
+    inp = nerf64.make_inputs(16, points, seed=points)
+    cast = {k: v.to(dtype).double() for k, v in inp.items()}
+    oracle = list(nerf64.reconstruct64_with_grads(cast["lengths"], cast["angles"], cast["dihedrals"], cast["grad"]))
+    ref = grads_of(ref_kernels.ref_reconstruct, inp, dtype, False)
+    ours = grads_of(cufk.reconstruct, inp, dtype, False)
+    rx, rg = errors(ref, oracle)
+    ox, og = errors(ours, oracle)
+    assert ox <= rx and og <= rg, {"ours": (ox, og), "reference": (rx, rg)}
+
+
+@pytest.mark.skipif(not ref_kernels.available("torsion"), reason="reference torsion kernel not built")
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_torsion_against_reference(dtype):
+    inp = nerf64.make_torsion_inputs(32, 768, seed=3)
+    raw = inp["raw"].to(dtype)
+    grad = inp["grad"].to(dtype)
+    oracle = nerf64.torsion64_with_grads(raw.double(), grad.double(), nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES)
+
+    def run(fn):
+        r = raw.cuda().requires_grad_(True)
+        xyz = fn(r)
+        xyz.backward(grad.cuda())
+        return xyz.detach().double().cpu(), r.grad.double().cpu()
+
+    ref = run(ref_kernels.ref_torsion)
+    ours = run(cufk.compile_torsion(nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES))
+    ex = lambda got: (float((got[0] - oracle[0]).abs().max()), float((got[1] - oracle[1]).norm() / oracle[1].norm()))
+    rx, rg = ex(ref)
+    ox, og = ex(ours)
+    if dtype == torch.float32:
+        assert rx <= 5e-4 and rg <= 1e-4, (rx, rg)
+        assert ox <= 5e-4 and og <= 1e-4, (ox, og)
+    else:
+        assert ox <= rx and og <= rg, {"ours": (ox, og), "reference": (rx, rg)}
