@@ -87,7 +87,7 @@ def build_extension(force: bool = False, verbose: bool = False) -> Path:
     )
     built = BUILD / "_C.so"
     tmp = EXT.with_suffix(".so.tmp")
-    shutil.copy2(built, tmp)
+    shutil.copy(built, tmp)  # fresh mtime: the artefact is newer than libcufkb.so it was linked against
     os.replace(tmp, EXT)
     return EXT
 

@@ -19,20 +19,37 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kTargetItems = 24;       // steps per thread when the batch alone fills the GPU
-constexpr int kMinItems = 5;           // never split a chain below this many steps per thread
-constexpr int kTargetWarpsPerSm = 16;  // resident warps per SM the plan aims for
+constexpr int kNumKernels = 16;
+constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
+constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
+#ifndef CUFKB_TARGET_WARPS_PER_SM
+#define CUFKB_TARGET_WARPS_PER_SM 20
+#endif
+constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;  // resident warps per SM the plan aims for
 
 struct DeviceCache {
   std::once_flag once;
   int sm_count = 0;
-  int max_smem_optin = 0;
+  int max_smem_optin = 0;     // per block, static + dynamic
+  int smem_per_sm = 0;        // per SM, all blocks
+  int reserved_per_block = 0; // runtime reservation per resident block
+  int regs_per_sm = 0;
+  int max_warps_per_sm = 0;
+  int max_blocks_per_sm = 0;
   int error = 0;
 };
 DeviceCache g_devices[kMaxDevices];
 
-// One bit per device: the kernel's dynamic shared-memory limit has been raised there.
-std::atomic<uint64_t> g_attr_done[16];
+// Per kernel: its register and static shared-memory footprint, and one bit per device saying that
+// its dynamic shared-memory limit has been raised there.
+struct KernelCache {
+  std::once_flag once;
+  int regs = 0;
+  int static_smem = 0;
+  int error = 0;
+  std::atomic<uint64_t> attr_done{0};
+};
+KernelCache g_kernels[kNumKernels];
 
 int current_device(int* dev) {
   const cudaError_t e = cudaGetDevice(dev);
@@ -44,9 +61,27 @@ int current_device(int* dev) {
 const DeviceCache* device_cache(int dev) {
   DeviceCache& d = g_devices[dev];
   std::call_once(d.once, [&] {
-    cudaError_t e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    d.error = static_cast<int>(e);
+    int warps_threads = 0;
+    const struct {
+      int* out;
+      cudaDeviceAttr attr;
+    } queries[] = {
+        {&d.sm_count, cudaDevAttrMultiProcessorCount},
+        {&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin},
+        {&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor},
+        {&d.reserved_per_block, cudaDevAttrReservedSharedMemoryPerBlock},
+        {&d.regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor},
+        {&warps_threads, cudaDevAttrMaxThreadsPerMultiProcessor},
+        {&d.max_blocks_per_sm, cudaDevAttrMaxBlocksPerMultiprocessor},
+    };
+    for (const auto& q : queries) {
+      const cudaError_t e = cudaDeviceGetAttribute(q.out, q.attr, dev);
+      if (e != cudaSuccess) {
+        d.error = static_cast<int>(e);
+        return;
+      }
+    }
+    d.max_warps_per_sm = warps_threads / cufkb::kWarp;
   });
   return &d;
 }
@@ -57,32 +92,67 @@ int fail_cuda(cudaError_t e) {
 }
 
 template <typename Kernel>
-cudaError_t ensure_smem_limit(Kernel kernel, int kernel_id, int dev, int max_optin) {
+const KernelCache* kernel_cache(Kernel kernel, int kernel_id) {
+  KernelCache& k = g_kernels[kernel_id];
+  std::call_once(k.once, [&] {
+    cudaFuncAttributes attr;
+    const cudaError_t e = cudaFuncGetAttributes(&attr, kernel);
+    if (e != cudaSuccess) {
+      k.error = static_cast<int>(e);
+      return;
+    }
+    k.regs = attr.numRegs;
+    k.static_smem = static_cast<int>(attr.sharedSizeBytes);
+  });
+  return &k;
+}
+
+template <typename Kernel>
+cudaError_t ensure_smem_limit(Kernel kernel, KernelCache* k, int dev, int max_optin) {
   const uint64_t bit = uint64_t(1) << dev;
-  if (g_attr_done[kernel_id].load(std::memory_order_acquire) & bit) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin);
-  if (e == cudaSuccess) g_attr_done[kernel_id].fetch_or(bit, std::memory_order_acq_rel);
+  if (k->attr_done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  // the opt-in maximum covers static + dynamic shared memory of a block
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin - k->static_smem);
+  if (e == cudaSuccess) k->attr_done.fetch_or(bit, std::memory_order_acq_rel);
   return e;
 }
 
 int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
-// Warps per chain and steps per thread.  Long chains get more warps so a thread keeps about
-// kTargetItems steps; small batches get more warps per chain (down to kMinItems steps per thread)
-// so that the grid still offers ~kTargetWarpsPerSm warps per SM.  K is made odd so that the
+// Warps per chain (W) and steps per thread (K).  A chain needs W >= ceil(steps / (32 kTargetItems))
+// so that a thread walks at most ~kTargetItems steps.  Beyond that, W grows while the SM would hold
+// fewer than kTargetWarpsPerSm resident warps (shared memory per chain and registers per thread
+// bound the resident chains), and while the whole grid offers fewer than that many warps per SM
+// (small batches), as long as a thread keeps >= kMinItems steps.  K is made odd so that the
 // threads' slot strides (3K words) fall on 32 distinct shared-memory banks.
 struct Plan {
   int threads;
   int items;
 };
 
-Plan make_plan(int64_t batch, int points, int sm_count) {
+int resident_warps(const DeviceCache& d, const KernelCache& k, size_t dyn_smem, int warps) {
+  const int chain_smem = static_cast<int>(dyn_smem) + k.static_smem + d.reserved_per_block;
+  int chains = chain_smem > 0 ? d.smem_per_sm / chain_smem : d.max_blocks_per_sm;
+  const int regs_per_warp = ((k.regs + 7) / 8) * 8 * cufkb::kWarp;
+  const int by_regs = regs_per_warp > 0 ? d.regs_per_sm / (regs_per_warp * warps) : chains;
+  if (by_regs < chains) chains = by_regs;
+  if (d.max_blocks_per_sm < chains) chains = d.max_blocks_per_sm;
+  if (d.max_warps_per_sm / warps < chains) chains = d.max_warps_per_sm / warps;
+  return chains * warps;
+}
+
+Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCache& k, size_t dyn_smem) {
   const int steps = points - 3;
   int warps = ceil_div(steps, cufkb::kWarp * kTargetItems);
   if (warps < 1) warps = 1;
   if (warps > cufkb::kMaxWarps) warps = cufkb::kMaxWarps;
-  const int64_t target = int64_t(sm_count) * kTargetWarpsPerSm;
-  while (warps < cufkb::kMaxWarps && batch * warps < target && ceil_div(steps, cufkb::kWarp * (warps + 1)) >= kMinItems) ++warps;
+  auto splittable = [&](int w) { return w < cufkb::kMaxWarps && ceil_div(steps, cufkb::kWarp * (w + 1)) >= kMinItems; };
+  while (splittable(warps) && resident_warps(d, k, dyn_smem, warps) < kTargetWarpsPerSm &&
+         resident_warps(d, k, dyn_smem, warps + 1) > resident_warps(d, k, dyn_smem, warps)) {
+    ++warps;
+  }
+  const int64_t grid_target = int64_t(d.sm_count) * kTargetWarpsPerSm;
+  while (splittable(warps) && batch * warps < grid_target) ++warps;
   int items = ceil_div(steps, cufkb::kWarp * warps);
   if ((items & 1) == 0) ++items;
   return {cufkb::kWarp * warps, items};
@@ -116,25 +186,32 @@ int check_shape(int dtype, int64_t batch, int64_t points) {
 struct LaunchEnv {
   int dev;
   const DeviceCache* cache;
+  Plan plan;
 };
 
-int launch_env(LaunchEnv* env) {
+// Device, kernel footprint, shared-memory opt-in and plan of one launch.
+template <typename Kernel>
+int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem) {
   const int e = current_device(&env->dev);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   env->cache = device_cache(env->dev);
   if (env->cache->error != 0) return fail_cuda(static_cast<cudaError_t>(env->cache->error));
+  const KernelCache* k = kernel_cache(kernel, kernel_id);
+  if (k->error != 0) return fail_cuda(static_cast<cudaError_t>(k->error));
+  if (static_cast<int>(smem) + k->static_smem > env->cache->max_smem_optin) return fail_cuda(cudaErrorInvalidValue);
+  if (cudaError_t err = ensure_smem_limit(kernel, &g_kernels[kernel_id], env->dev, env->cache->max_smem_optin)) return fail_cuda(err);
+  env->plan = make_plan(batch, points, *env->cache, *k, smem);
   return CUFKB_SUCCESS;
 }
 
 template <typename T>
 int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz,
                        int64_t batch, int points, cudaStream_t stream, int kernel_id) {
-  LaunchEnv env;
-  if (int st = launch_env(&env)) return st;
-  const Plan plan = make_plan(batch, points, env.cache->sm_count);
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
-  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
+  const Plan plan = env.plan;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{points, points - 3, plan.items};
@@ -146,12 +223,11 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
 template <typename T>
 int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g,
                         void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
-  LaunchEnv env;
-  if (int st = launch_env(&env)) return st;
-  const Plan plan = make_plan(batch, points, env.cache->sm_count);
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_kernel<T>;
-  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
+  const Plan plan = env.plan;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{points, points - 3, plan.items};
@@ -176,12 +252,11 @@ template <typename T>
 int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
                          cudaStream_t stream, int kernel_id) {
   using R = typename cufkb::ComputeOf<T>::type;
-  LaunchEnv env;
-  if (int st = launch_env(&env)) return st;
-  const Plan plan = make_plan(batch, points, env.cache->sm_count);
   const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
   auto kernel = cufkb::torsion_forward_kernel<T>;
-  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
+  const Plan plan = env.plan;
   const ChainGeometry geo{points, points - 3, plan.items};
   kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                        static_cast<T*>(xyz), geo);
@@ -193,12 +268,11 @@ template <typename T>
 int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw,
                           int64_t grad_stride, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
   using R = typename cufkb::ComputeOf<T>::type;
-  LaunchEnv env;
-  if (int st = launch_env(&env)) return st;
-  const Plan plan = make_plan(batch, points, env.cache->sm_count);
   const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
   auto kernel = cufkb::torsion_backward_kernel<T>;
-  if (cudaError_t e = ensure_smem_limit(kernel, kernel_id, env.dev, env.cache->max_smem_optin)) return fail_cuda(e);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
+  const Plan plan = env.plan;
   const ChainGeometry geo{points, points - 3, plan.items};
   kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                        static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);

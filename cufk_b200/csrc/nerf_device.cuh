@@ -26,6 +26,8 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "nerf_math.cuh"
+
 namespace cufkb {
 
 constexpr int kWarp = 32;
@@ -65,7 +67,15 @@ __device__ __forceinline__ T from_r(R x) {
   }
 }
 
-__device__ __forceinline__ void sin_cos(float x, float& s, float& c) { sincosf(x, &s, &c); }
+// Angles of real chains take the short reduction of nerf_math.cuh; anything beyond its range (or
+// NaN/inf) takes the CUDA library routine.  float64 always uses the library routine.
+__device__ __forceinline__ void sin_cos(float x, float& s, float& c) {
+  if (fabsf(x) <= kSinCosFastRange) {
+    sincos_fast(x, s, c);
+  } else {
+    sincosf(x, &s, &c);
+  }
+}
 __device__ __forceinline__ void sin_cos(double x, double& s, double& c) { sincos(x, &s, &c); }
 __device__ __forceinline__ float sqrt_r(float x) { return sqrtf(x); }
 __device__ __forceinline__ double sqrt_r(double x) { return sqrt(x); }
@@ -346,10 +356,10 @@ __device__ __forceinline__ void cross3(const R* a, const R* b, R* out) {
 template <typename R>
 __device__ __forceinline__ void normalize3(R* v) {
   const R n2 = dot3(v, v);
-  const R d = sqrt_r(max_r(n2, static_cast<R>(1.0e-12f)));
-  v[0] = v[0] / d;
-  v[1] = v[1] / d;
-  v[2] = v[2] / d;
+  const R inv = R(1) / sqrt_r(max_r(n2, static_cast<R>(1.0e-12f)));
+  v[0] *= inv;
+  v[1] *= inv;
+  v[2] *= inv;
 }
 
 template <typename R, typename T>

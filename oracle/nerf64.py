@@ -317,26 +317,35 @@ def _torsion_nerf(L, st, ct, S, C, l0, l1, sc0):
 
 
 def torsion64_with_grads(raw, grad_xyz, bond_lengths, bond_angles):
-    """Forward plus the reference's raw-pair chain rule (torsion.cu:173-182).
+    """Forward plus the reference's torsion backward (torsion.cu:173-217), in float64.
 
-    d/dphi is taken along the unit circle from autograd w.r.t. the normalised (S, C):
-    dphi = dL/dS * C - dL/dC * S; then d raw = dphi * (c_raw, -s_raw) / max(s^2 + c^2, 1e-16).
+    World-space force/moment form of world_torsion_grad (torsion.cu:213-217): with F = sum_{j>=k+3} g_j
+    and M = sum_{j>=k+3} x_j x g_j, d phi_k = ((x_{k+2} - x_{k+1}) / len_{(k+1)%3}) . (M - x_{k+2} x F);
+    then the raw-pair chain rule d raw = d phi * (c_raw, -s_raw) / max(s^2 + c^2, 1e-16)
+    (store_raw_pair_grad, torsion.cu:173-182).  For unclamped pairs this equals the derivative of
+    the forward through atan2 (checked in tests/test_oracle.py).
     """
     b, width = raw.shape
     steps = width // 2
     S, C, n2 = normalize_pairs64(raw)
-    S = S.clone().requires_grad_(True)
-    C = C.clone().requires_grad_(True)
     L, st, ct, l0, l1, a0, sincos = _torsion_tiles(bond_lengths, bond_angles, b, steps)
     xyz = _torsion_nerf(L, st, ct, S, C, l0, l1, sincos[0])
-    gS, gC = torch.autograd.grad(xyz, (S, C), grad_xyz.to(F64))
-    dphi = gS * C.detach() - gC * S.detach()
+    g = grad_xyz.to(F64)
+    lengths, _ = torsion_constants(bond_lengths, bond_angles)
+    force = torch.flip(torch.cumsum(torch.flip(g, [1]), 1), [1])  # force[:, j] = sum_{i>=j} g_i
+    moment = torch.flip(torch.cumsum(torch.flip(torch.linalg.cross(xyz, g, dim=-1), [1]), 1), [1])
+    k = torch.arange(steps)
+    prev, pivot = xyz[:, k + 1], xyz[:, k + 2]
+    Fk, Mk = force[:, k + 3], moment[:, k + 3]
+    inv_len = 1.0 / torch.tensor(lengths, dtype=F64)[(k + 1) % 3]
+    tau = Mk - torch.linalg.cross(pivot, Fk, dim=-1)
+    dphi = inv_len * ((pivot - prev) * tau).sum(-1)
     rs = raw[:, 0::2].to(F64)
     rc = raw[:, 1::2].to(F64)
     grad = torch.empty(b, width, dtype=F64)
     grad[:, 0::2] = dphi * rc / n2
     grad[:, 1::2] = -dphi * rs / n2
-    return xyz.detach(), grad
+    return xyz, grad
 
 
 # ---------------------------------------------------------------------------------------------
