@@ -19,7 +19,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 16;
+constexpr int kNumKernels = 32;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 #ifndef CUFKB_TARGET_WARPS_PER_SM
@@ -204,35 +204,60 @@ int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int 
   return CUFKB_SUCCESS;
 }
 
+// Chains per CTA: two float chains share a CTA (float2 lanes, packed f32x2 arithmetic) when the
+// batch still gives every SM several CTAs; float64 and small batches use one chain per CTA.
+#ifndef CUFKB_PAIR_MIN_CTAS_PER_SM
+#define CUFKB_PAIR_MIN_CTAS_PER_SM 4
+#endif
 template <typename T>
-int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz,
-                       int64_t batch, int points, cudaStream_t stream, int kernel_id) {
-  const size_t smem = cufkb::block_smem_bytes<T>(points, false);
-  auto kernel = cufkb::block_forward_kernel<T>;
+bool use_pairs(int64_t batch, const DeviceCache& d) {
+  if constexpr (std::is_same_v<T, double>) {
+    return false;
+  } else {
+    return batch / 2 >= int64_t(d.sm_count) * CUFKB_PAIR_MIN_CTAS_PER_SM;
+  }
+}
+
+// Kernel ids for the caches: kind (4) x dtype (4) x chains per CTA (2).
+constexpr int kernel_id(int kind, int dtype, int chains) { return (kind * 4 + dtype) * 2 + (chains - 1); }
+
+template <typename T>
+constexpr int dtype_index() {
+  if constexpr (std::is_same_v<T, float>) return 0;
+  if constexpr (std::is_same_v<T, double>) return 1;
+  if constexpr (std::is_same_v<T, __half>) return 2;
+  return 3;
+}
+
+template <typename T, int kC>
+int block_forward_launch(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
+                         int points, cudaStream_t stream) {
+  const size_t smem = kC * cufkb::block_region_bytes<T>(points, false);
+  auto kernel = cufkb::block_forward_kernel<T, kC>;
+  const int64_t ctas = (batch + kC - 1) / kC;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
-  const Plan plan = env.plan;
+  if (int st = launch_env(&env, kernel, kernel_id(0, dtype_index<T>(), kC), ctas, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{points, points - 3, plan.items};
-  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
-template <typename T>
-int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g,
-                        void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
-  const size_t smem = cufkb::block_smem_bytes<T>(points, true);
-  auto kernel = cufkb::block_backward_kernel<T>;
+template <typename T, int kC>
+int block_backward_launch(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL,
+                          void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
+  const size_t smem = kC * cufkb::block_region_bytes<T>(points, true);
+  auto kernel = cufkb::block_backward_kernel<T, kC>;
+  const int64_t ctas = (batch + kC - 1) / kC;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
-  const Plan plan = env.plan;
+  if (int st = launch_env(&env, kernel, kernel_id(1, dtype_index<T>(), kC), ctas, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{points, points - 3, plan.items};
-  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL),
-                                                                       static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
+                                                                          static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
@@ -248,36 +273,94 @@ cufkb::TorsionConsts<R> torsion_consts(const cufkb_torsion_constants* c) {
   return out;
 }
 
-template <typename T>
-int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
-                         cudaStream_t stream, int kernel_id) {
+template <typename T, int kC>
+int torsion_forward_launch(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
+                           cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
-  const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
-  auto kernel = cufkb::torsion_forward_kernel<T>;
+  const size_t smem = kC * cufkb::torsion_region_bytes<T>(points, false);
+  auto kernel = cufkb::torsion_forward_kernel<T, kC>;
+  const int64_t ctas = (batch + kC - 1) / kC;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
-  const Plan plan = env.plan;
-  const ChainGeometry geo{points, points - 3, plan.items};
-  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
-                                                                       static_cast<T*>(xyz), geo);
+  if (int st = launch_env(&env, kernel, kernel_id(2, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                          static_cast<T*>(xyz), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
-template <typename T>
-int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw,
-                          int64_t grad_stride, int64_t batch, int points, cudaStream_t stream, int kernel_id) {
+template <typename T, int kC>
+int torsion_backward_launch(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw, int64_t grad_stride,
+                            int64_t batch, int points, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
-  const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
-  auto kernel = cufkb::torsion_backward_kernel<T>;
+  const size_t smem = kC * cufkb::torsion_region_bytes<T>(points, true);
+  auto kernel = cufkb::torsion_backward_kernel<T, kC>;
+  const int64_t ctas = (batch + kC - 1) / kC;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id, batch, points, smem)) return st;
-  const Plan plan = env.plan;
-  const ChainGeometry geo{points, points - 3, plan.items};
-  kernel<<<static_cast<unsigned>(batch), plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
-                                                                       static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
+  if (int st = launch_env(&env, kernel, kernel_id(3, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                          static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
+}
+
+// Dispatch on chains per CTA (needs the device attributes, hence the current-device lookup).
+template <typename T, typename Fn1, typename Fn2>
+int with_pairs(int64_t batch, Fn1 single, Fn2 pair) {
+  int dev = 0;
+  if (int e = current_device(&dev)) return fail_cuda(static_cast<cudaError_t>(e));
+  const DeviceCache* d = device_cache(dev);
+  if (d->error != 0) return fail_cuda(static_cast<cudaError_t>(d->error));
+  return use_pairs<T>(batch, *d) ? pair() : single();
+}
+
+template <typename T>
+int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
+                       int points, cudaStream_t s) {
+  if constexpr (std::is_same_v<T, double>) {
+    return block_forward_launch<T, 1>(L, A, D, p0, fd, nn, xyz, batch, points, s);
+  } else {
+    return with_pairs<T>(
+        batch, [&] { return block_forward_launch<T, 1>(L, A, D, p0, fd, nn, xyz, batch, points, s); },
+        [&] { return block_forward_launch<T, 2>(L, A, D, p0, fd, nn, xyz, batch, points, s); });
+  }
+}
+
+template <typename T>
+int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL,
+                        void* gA, void* gD, int64_t batch, int points, cudaStream_t s) {
+  if constexpr (std::is_same_v<T, double>) {
+    return block_backward_launch<T, 1>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s);
+  } else {
+    return with_pairs<T>(
+        batch, [&] { return block_backward_launch<T, 1>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s); },
+        [&] { return block_backward_launch<T, 2>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s); });
+  }
+}
+
+template <typename T>
+int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
+                         cudaStream_t s) {
+  if constexpr (std::is_same_v<T, double>) {
+    return torsion_forward_launch<T, 1>(raw, raw_stride, c, xyz, batch, points, s);
+  } else {
+    return with_pairs<T>(
+        batch, [&] { return torsion_forward_launch<T, 1>(raw, raw_stride, c, xyz, batch, points, s); },
+        [&] { return torsion_forward_launch<T, 2>(raw, raw_stride, c, xyz, batch, points, s); });
+  }
+}
+
+template <typename T>
+int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw, int64_t grad_stride,
+                          int64_t batch, int points, cudaStream_t s) {
+  if constexpr (std::is_same_v<T, double>) {
+    return torsion_backward_launch<T, 1>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s);
+  } else {
+    return with_pairs<T>(
+        batch, [&] { return torsion_backward_launch<T, 1>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s); },
+        [&] { return torsion_backward_launch<T, 2>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s); });
+  }
 }
 
 }  // namespace
@@ -300,13 +383,13 @@ int cufkb_block_forward(int dtype, const void* lengths, const void* angles, cons
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_forward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 0);
+      return block_forward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
     case CUFKB_FLOAT64:
-      return block_forward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 1);
+      return block_forward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
     case CUFKB_FLOAT16:
-      return block_forward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 2);
+      return block_forward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
     default:
-      return block_forward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s, 3);
+      return block_forward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
   }
 }
 
@@ -326,16 +409,16 @@ int cufkb_block_backward(int dtype, const void* lengths, const void* angles, con
   switch (dtype) {
     case CUFKB_FLOAT32:
       return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                        grad_angles, grad_dihedrals, batch, n, s, 4);
+                                        grad_angles, grad_dihedrals, batch, n, s);
     case CUFKB_FLOAT64:
       return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                         grad_angles, grad_dihedrals, batch, n, s, 5);
+                                         grad_angles, grad_dihedrals, batch, n, s);
     case CUFKB_FLOAT16:
       return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                         grad_angles, grad_dihedrals, batch, n, s, 6);
+                                         grad_angles, grad_dihedrals, batch, n, s);
     default:
       return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz,
-                                                grad_lengths, grad_angles, grad_dihedrals, batch, n, s, 7);
+                                                grad_lengths, grad_angles, grad_dihedrals, batch, n, s);
   }
 }
 
@@ -352,13 +435,13 @@ int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stri
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return torsion_forward_impl<float>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 8);
+      return torsion_forward_impl<float>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s);
     case CUFKB_FLOAT64:
-      return torsion_forward_impl<double>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 9);
+      return torsion_forward_impl<double>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s);
     case CUFKB_FLOAT16:
-      return torsion_forward_impl<__half>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 10);
+      return torsion_forward_impl<__half>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s);
     default:
-      return torsion_forward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, 11);
+      return torsion_forward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s);
   }
 }
 
@@ -376,16 +459,14 @@ int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_str
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return torsion_backward_impl<float>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s, 12);
+      return torsion_backward_impl<float>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
     case CUFKB_FLOAT64:
-      return torsion_backward_impl<double>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s,
-                                           13);
+      return torsion_backward_impl<double>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
     case CUFKB_FLOAT16:
-      return torsion_backward_impl<__half>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s,
-                                           14);
+      return torsion_backward_impl<__half>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
     default:
       return torsion_backward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch,
-                                                  n, s, 15);
+                                                  n, s);
   }
 }
 

@@ -1,20 +1,23 @@
 // Device-side building blocks of the sm_100a NeRF chain kernels.
 //
 // Layout conventions used by every kernel in this library:
-//   * one CTA reconstructs one chain; its W warps own consecutive runs of K steps per lane
-//     (lane-major: thread t owns steps [t*K, t*K + K)), K odd so that the lanes' shared-memory
-//     strides (3K words) hit 32 distinct banks;
+//   * one CTA reconstructs C = 1 or 2 chains; its W warps own consecutive runs of K steps per lane
+//     (thread t owns steps [t*K, t*K + K) of every chain of the CTA), K odd so that the lanes'
+//     shared-memory strides (3K words) hit 32 distinct banks;
 //   * a chain's per-atom data lives in shared memory as "slots": atom a owns the three words
 //     X[3a..3a+2].  Inputs are scattered into the slot of the atom they place (length L[i] ->
 //     X[3(i+1)], angle A[i] -> X[3(i+2)+1], dihedral D[i] -> X[3(i+3)+2]), so that step s reads
 //     its (L[s+2], A[s+1], D[s]) from slot s+3 and can overwrite it in place with its result:
 //     the xyz of atom s+3 in the forward, the three parameter gradients in the backward.  The slot
-//     array then has exactly the layout of the (N, 3) output row.
+//     array then has exactly the layout of the (N, 3) output row;
+//   * arithmetic runs on a lane type V: float (one float chain per CTA), float2 (two float chains
+//     per CTA, chain 0 in .x and chain 1 in .y, so that every multiply-add is one packed sm_100
+//     f32x2 instruction for both chains) or double.
 //
 // Reference behaviour restated here (paths relative to the cufk project root):
 //   * local transform R rows [(-c,-s,0), (sC,-cC,-S), (sS,-cS,C)], t = l R[:,0]
-//     (src/cufk/csrc/affine.cuh:36-51), applied as P <- P Rx(phi) Mz(theta) which is the same
-//     product written as two plane rotations;
+//     (src/cufk/csrc/affine.cuh:36-51), applied as P <- P Rx(phi) Mz(theta), the same product
+//     written as two plane rotations;
 //   * affine compose (R1,t1)(R2,t2) = (R1 R2, t1 + R1 t2) (affine.cuh:53-58);
 //   * first frame (src/cufk/csrc/block.cu:113-148, frame_utils.cuh:17-31).
 #pragma once
@@ -67,29 +70,120 @@ __device__ __forceinline__ T from_r(R x) {
   }
 }
 
-// Angles of real chains take the short reduction of nerf_math.cuh; anything beyond its range (or
-// NaN/inf) takes the CUDA library routine.  float64 always uses the library routine.
-__device__ __forceinline__ void sin_cos(float x, float& s, float& c) {
-  if (fabsf(x) <= kSinCosFastRange) {
-    sincos_fast(x, s, c);
+// ------------------------------------------------------------------------------------------
+// lane arithmetic: V = float | float2 | double
+// ------------------------------------------------------------------------------------------
+template <typename V>
+struct Lanes;
+template <>
+struct Lanes<float> {
+  using S = float;
+  static constexpr int kCount = 1;
+};
+template <>
+struct Lanes<float2> {
+  using S = float;
+  static constexpr int kCount = 2;
+};
+template <>
+struct Lanes<double> {
+  using S = double;
+  static constexpr int kCount = 1;
+};
+
+__device__ __forceinline__ float vfma(float a, float b, float c) { return fmaf(a, b, c); }
+__device__ __forceinline__ double vfma(double a, double b, double c) { return fma(a, b, c); }
+__device__ __forceinline__ float2 vfma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float vmul(float a, float b) { return a * b; }
+__device__ __forceinline__ double vmul(double a, double b) { return a * b; }
+__device__ __forceinline__ float2 vmul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float vadd(float a, float b) { return a + b; }
+__device__ __forceinline__ double vadd(double a, double b) { return a + b; }
+__device__ __forceinline__ float2 vadd(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float vneg(float a) { return -a; }
+__device__ __forceinline__ double vneg(double a) { return -a; }
+__device__ __forceinline__ float2 vneg(float2 a) { return make_float2(-a.x, -a.y); }
+// a - b
+__device__ __forceinline__ float vsub(float a, float b) { return a - b; }
+__device__ __forceinline__ double vsub(double a, double b) { return a - b; }
+__device__ __forceinline__ float2 vsub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
+
+template <typename V>
+__device__ __forceinline__ V splat(typename Lanes<V>::S x) {
+  if constexpr (std::is_same_v<V, float2>) {
+    return make_float2(x, x);
   } else {
-    sincosf(x, &s, &c);
+    return x;
   }
 }
-__device__ __forceinline__ void sin_cos(double x, double& s, double& c) { sincos(x, &s, &c); }
-__device__ __forceinline__ float sqrt_r(float x) { return sqrtf(x); }
-__device__ __forceinline__ double sqrt_r(double x) { return sqrt(x); }
-__device__ __forceinline__ float max_r(float a, float b) { return fmaxf(a, b); }
-__device__ __forceinline__ double max_r(double a, double b) { return fmax(a, b); }
-__device__ __forceinline__ float abs_r(float a) { return fabsf(a); }
-__device__ __forceinline__ double abs_r(double a) { return fabs(a); }
+
+template <typename V>
+__device__ __forceinline__ typename Lanes<V>::S lane(const V& v, int i) {
+  if constexpr (std::is_same_v<V, float2>) {
+    return i == 0 ? v.x : v.y;
+  } else {
+    return v;
+  }
+}
+
+// per-lane helpers for the rare non-multiply-add operations
+template <typename V, typename Fn>
+__device__ __forceinline__ V lanewise(const V& a, Fn fn) {
+  if constexpr (std::is_same_v<V, float2>) {
+    return make_float2(fn(a.x), fn(a.y));
+  } else {
+    return fn(a);
+  }
+}
+
+template <typename V>
+__device__ __forceinline__ V vrecip_sqrt_clamped(V n2) {
+  return lanewise(n2, [](auto x) {
+    using S = decltype(x);
+    return S(1) / sqrt(x > static_cast<S>(1.0e-12f) ? x : static_cast<S>(1.0e-12f));
+  });
+}
+
+// sine and cosine of an angle pair (one step: bond angle and dihedral).  Float angles of real chains
+// take the packed short reduction of nerf_math.cuh; anything beyond its range (or NaN/inf) takes
+// the CUDA library routine for that step.  float64 always uses the library routine.
+__device__ __forceinline__ bool fast_range(float x) { return fabsf(x) <= kSinCosFastRange; }
+
+__device__ __forceinline__ void step_sincos(float th, float ph, float& st, float& ct, float& sp, float& cp) {
+  if (fast_range(th) && fast_range(ph)) {
+    float2 s, c;
+    sincos_fast2(make_float2(th, ph), s, c);
+    st = s.x;
+    ct = c.x;
+    sp = s.y;
+    cp = c.y;
+  } else {
+    sincosf(th, &st, &ct);
+    sincosf(ph, &sp, &cp);
+  }
+}
+
+__device__ __forceinline__ void step_sincos(float2 th, float2 ph, float2& st, float2& ct, float2& sp, float2& cp) {
+  if (fast_range(th.x) && fast_range(th.y) && fast_range(ph.x) && fast_range(ph.y)) {
+    sincos_fast2(th, st, ct);
+    sincos_fast2(ph, sp, cp);
+  } else {
+    sincosf(th.x, &st.x, &ct.x);
+    sincosf(th.y, &st.y, &ct.y);
+    sincosf(ph.x, &sp.x, &cp.x);
+    sincosf(ph.y, &sp.y, &cp.y);
+  }
+}
+
+__device__ __forceinline__ void step_sincos(double th, double ph, double& st, double& ct, double& sp, double& cp) {
+  sincos(th, &st, &ct);
+  sincos(ph, &sp, &cp);
+}
 
 // ------------------------------------------------------------------------------------------
 // async copies (sm_80+ LDGSTS for scattered elements, sm_90+ bulk copy engine for stores)
 // ------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 template <int Bytes>
 __device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {
@@ -97,8 +191,7 @@ __device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {
   if constexpr (Bytes == 16) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
   } else {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "n"(Bytes)
-                 : "memory");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "n"(Bytes) : "memory");
   }
 }
 
@@ -108,14 +201,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 
 // One bulk (TMA engine) store of a 16-byte aligned, 16-byte multiple range from shared memory.
 __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gmem_dst), "r"(smem_u32(smem_src)),
-               "r"(bytes)
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gmem_dst), "r"(smem_u32(smem_src)), "r"(bytes)
                : "memory");
   asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
 }
 
-// Waits until every committed bulk store has finished READING shared memory (the CTA may then
-// exit or reuse the buffer; the global writes complete on their own).
+// Waits until every committed bulk store of this thread has finished READING shared memory (the
+// CTA may then exit or reuse the buffer; the global writes complete on their own).
 __device__ __forceinline__ void bulk_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
 
 // Copies a contiguous global range of `count` elements into shared memory so that the shared
@@ -132,9 +224,10 @@ __device__ __forceinline__ T* stage_row_async(unsigned char* smem_base16, const 
     const int head = static_cast<int>((a0 - g0) / sizeof(T));
     const int chunks = static_cast<int>((a1 - a0) / 16u);
     const int tail0 = static_cast<int>((a1 - g0) / sizeof(T));
-    for (int c = tid; c < chunks; c += nthreads) {
-      cp_async<16>(reinterpret_cast<unsigned char*>(dst + head) + 16 * c, reinterpret_cast<const unsigned char*>(a0) + 16 * c);
-    }
+    unsigned char* d = reinterpret_cast<unsigned char*>(dst + head);
+    const unsigned char* s = reinterpret_cast<const unsigned char*>(a0);
+#pragma unroll 4
+    for (int c = tid; c < chunks; c += nthreads) cp_async<16>(d + 16 * c, s + 16 * c);
     for (int i = tid; i < head; i += nthreads) dst[i] = gsrc[i];
     for (int i = tail0 + tid; i < count; i += nthreads) dst[i] = gsrc[i];
   } else {
@@ -146,12 +239,12 @@ __device__ __forceinline__ T* stage_row_async(unsigned char* smem_base16, const 
 // Bytes of shared memory reserved for a row staged by stage_row_async.
 __host__ __device__ constexpr size_t staged_row_bytes(size_t count, size_t elem) { return ((count * elem + 15) & ~size_t(15)) + 16; }
 
-// Writes `count` elements of shared memory (laid out with the same address residue mod 16 as
-// the destination) to global memory: one bulk store for the aligned interior, plain stores for the
-// ragged ends.  Every thread of the CTA calls it after a barrier that follows the last shared
-// write; `fence.proxy.async` orders those generic-proxy writes before the bulk engine reads them.
+// Writes `count` elements of shared memory (laid out with the same address residue mod 16 as the
+// destination) to global memory: one bulk store for the aligned interior, issued by `issuer`, plain
+// stores for the ragged ends.  Every thread of the CTA calls it after a barrier that follows the last
+// shared write; `fence.proxy.async` orders those generic-proxy writes before the bulk engine reads.
 template <typename T>
-__device__ __forceinline__ void store_row_bulk(T* gdst, const T* ssrc, int count, int tid, int nthreads) {
+__device__ __forceinline__ void store_row_bulk(T* gdst, const T* ssrc, int count, int tid, int nthreads, int issuer) {
   const uintptr_t g0 = reinterpret_cast<uintptr_t>(gdst);
   const uintptr_t g1 = g0 + static_cast<uintptr_t>(count) * sizeof(T);
   const uintptr_t a0 = (g0 + 15u) & ~uintptr_t(15);
@@ -159,12 +252,9 @@ __device__ __forceinline__ void store_row_bulk(T* gdst, const T* ssrc, int count
   if (a1 > a0) {
     const int head = static_cast<int>((a0 - g0) / sizeof(T));
     const int tail0 = static_cast<int>((a1 - g0) / sizeof(T));
-    if (tid == 0) {
-      bulk_store(reinterpret_cast<void*>(a0), ssrc + head, static_cast<uint32_t>(a1 - a0));
-    }
+    if (tid == issuer) bulk_store(reinterpret_cast<void*>(a0), ssrc + head, static_cast<uint32_t>(a1 - a0));
     for (int i = tid; i < head; i += nthreads) gdst[i] = ssrc[i];
     for (int i = tail0 + tid; i < count; i += nthreads) gdst[i] = ssrc[i];
-    if (tid == 0) bulk_store_wait_read();
   } else {
     for (int i = tid; i < count; i += nthreads) gdst[i] = ssrc[i];
   }
@@ -173,100 +263,117 @@ __device__ __forceinline__ void store_row_bulk(T* gdst, const T* ssrc, int count
 // ------------------------------------------------------------------------------------------
 // affine frames in registers
 // ------------------------------------------------------------------------------------------
-template <typename R>
+template <typename V>
 struct Affine {
-  R m[9];  // row-major rotation
-  R v[3];  // translation
+  V m[9];  // row-major rotation
+  V v[3];  // translation
 };
 
-template <typename R>
-__device__ __forceinline__ Affine<R> affine_identity() {
-  Affine<R> a;
+template <typename V>
+__device__ __forceinline__ Affine<V> affine_identity() {
+  using S = typename Lanes<V>::S;
+  Affine<V> a;
 #pragma unroll
-  for (int i = 0; i < 9; ++i) a.m[i] = (i % 4 == 0) ? R(1) : R(0);
-  a.v[0] = a.v[1] = a.v[2] = R(0);
+  for (int i = 0; i < 9; ++i) a.m[i] = splat<V>((i % 4 == 0) ? S(1) : S(0));
+  a.v[0] = a.v[1] = a.v[2] = splat<V>(S(0));
   return a;
 }
 
 // (a.m, a.v)(b.m, b.v) = (a.m b.m, a.v + a.m b.v)
-template <typename R>
-__device__ __forceinline__ Affine<R> compose(const Affine<R>& a, const Affine<R>& b) {
-  Affine<R> r;
+template <typename V>
+__device__ __forceinline__ Affine<V> compose(const Affine<V>& a, const Affine<V>& b) {
+  Affine<V> r;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      r.m[3 * i + j] = a.m[3 * i + 0] * b.m[0 + j] + a.m[3 * i + 1] * b.m[3 + j] + a.m[3 * i + 2] * b.m[6 + j];
+      r.m[3 * i + j] = vfma(a.m[3 * i + 2], b.m[6 + j], vfma(a.m[3 * i + 1], b.m[3 + j], vmul(a.m[3 * i + 0], b.m[0 + j])));
     }
-    r.v[i] = a.v[i] + a.m[3 * i + 0] * b.v[0] + a.m[3 * i + 1] * b.v[1] + a.m[3 * i + 2] * b.v[2];
+    r.v[i] = vfma(a.m[3 * i + 2], b.v[2], vfma(a.m[3 * i + 1], b.v[1], vfma(a.m[3 * i + 0], b.v[0], a.v[i])));
   }
   return r;
+}
+
+// Precomputed per-step factors of the local transform: s, c of the bond angle and S, C of the
+// dihedral, with the negations the multiply-adds below need.
+template <typename V>
+struct StepRot {
+  V s, c, S, C, ns, nc, nS, l;
+};
+
+template <typename V>
+__device__ __forceinline__ StepRot<V> step_rot(V l, V s, V c, V S, V C) {
+  return {s, c, S, C, vneg(s), vneg(c), vneg(S), l};
 }
 
 // P <- P * L(l, theta, phi) with L = (Rx(phi) Mz(theta), l Rx(phi) Mz(theta) e_x):
 //   Rx(phi) = [[1,0,0],[0,C,-S],[0,S,C]],  Mz(theta) = [[-c,-s,0],[s,-c,0],[0,0,1]].
 // Their product is the reference's local rotation; the translation is l times the new first
-// column, so one step costs 27 multiply-adds.
-template <typename R>
-__device__ __forceinline__ void advance(Affine<R>& P, R l, R s, R c, R S, R C) {
+// column, so one step costs 27 multiply-adds (one instruction per multiply-add for both chains
+// of a float2 lane pair).
+template <typename V>
+__device__ __forceinline__ void advance(Affine<V>& P, const StepRot<V>& q) {
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
-    const R c0 = P.m[3 * r + 0];
-    const R c1 = P.m[3 * r + 1];
-    const R c2 = P.m[3 * r + 2];
-    const R y = C * c1 + S * c2;
-    const R z = C * c2 - S * c1;
-    const R x0 = s * y - c * c0;
-    const R y0 = -(s * c0 + c * y);
+    const V c0 = P.m[3 * r + 0];
+    const V c1 = P.m[3 * r + 1];
+    const V c2 = P.m[3 * r + 2];
+    const V y = vfma(q.S, c2, vmul(q.C, c1));       // C c1 + S c2
+    const V z = vfma(q.nS, c1, vmul(q.C, c2));      // C c2 - S c1
+    const V x0 = vfma(q.s, y, vmul(q.nc, c0));      // s y - c c0
+    const V y0 = vfma(q.ns, c0, vmul(q.nc, y));     // -s c0 - c y
     P.m[3 * r + 0] = x0;
     P.m[3 * r + 1] = y0;
     P.m[3 * r + 2] = z;
-    P.v[r] += l * x0;
+    P.v[r] = vfma(q.l, x0, P.v[r]);
   }
 }
 
-template <typename R>
-__device__ __forceinline__ R shfl_up_r(R x, int off) {
-  return __shfl_up_sync(0xffffffffu, x, off);
+__device__ __forceinline__ float shfl_up(float x, int off) { return __shfl_up_sync(0xffffffffu, x, off); }
+__device__ __forceinline__ double shfl_up(double x, int off) { return __shfl_up_sync(0xffffffffu, x, off); }
+__device__ __forceinline__ float2 shfl_up(float2 x, int off) {
+  return make_float2(__shfl_up_sync(0xffffffffu, x.x, off), __shfl_up_sync(0xffffffffu, x.y, off));
 }
-template <typename R>
-__device__ __forceinline__ R shfl_down_r(R x, int off) {
-  return __shfl_down_sync(0xffffffffu, x, off);
+__device__ __forceinline__ float shfl_down(float x, int off) { return __shfl_down_sync(0xffffffffu, x, off); }
+__device__ __forceinline__ double shfl_down(double x, int off) { return __shfl_down_sync(0xffffffffu, x, off); }
+__device__ __forceinline__ float2 shfl_down(float2 x, int off) {
+  return make_float2(__shfl_down_sync(0xffffffffu, x.x, off), __shfl_down_sync(0xffffffffu, x.y, off));
 }
-template <typename R>
-__device__ __forceinline__ R shfl_idx_r(R x, int src) {
-  return __shfl_sync(0xffffffffu, x, src);
+__device__ __forceinline__ float shfl_xor(float x, int m) { return __shfl_xor_sync(0xffffffffu, x, m); }
+__device__ __forceinline__ double shfl_xor(double x, int m) { return __shfl_xor_sync(0xffffffffu, x, m); }
+__device__ __forceinline__ float2 shfl_xor(float2 x, int m) {
+  return make_float2(__shfl_xor_sync(0xffffffffu, x.x, m), __shfl_xor_sync(0xffffffffu, x.y, m));
 }
 
-template <typename R>
-__device__ __forceinline__ Affine<R> shfl_up_affine(const Affine<R>& a, int off) {
-  Affine<R> r;
+template <typename V>
+__device__ __forceinline__ Affine<V> shfl_up_affine(const Affine<V>& a, int off) {
+  Affine<V> r;
 #pragma unroll
-  for (int i = 0; i < 9; ++i) r.m[i] = shfl_up_r(a.m[i], off);
+  for (int i = 0; i < 9; ++i) r.m[i] = shfl_up(a.m[i], off);
 #pragma unroll
-  for (int i = 0; i < 3; ++i) r.v[i] = shfl_up_r(a.v[i], off);
+  for (int i = 0; i < 3; ++i) r.v[i] = shfl_up(a.v[i], off);
   return r;
 }
 
-// Exclusive prefix (product of the totals of all lower threads of the CTA) of each thread's
-// affine total.  Warp level: Kogge-Stone over lanes; CTA level: warp totals through shared memory.
-template <typename R>
-__device__ __forceinline__ Affine<R> cta_exclusive_affine(const Affine<R>& total, Affine<R>* warp_totals, int nwarps) {
+// Exclusive prefix (product of the totals of all lower threads of the CTA) of each thread's affine
+// total.  Warp level: Kogge-Stone over lanes; CTA level: warp totals through shared memory.
+template <typename V>
+__device__ __forceinline__ Affine<V> cta_exclusive_affine(const Affine<V>& total, Affine<V>* warp_totals, int nwarps) {
   const int lane = threadIdx.x & (kWarp - 1);
   const int warp = threadIdx.x / kWarp;
-  Affine<R> x = total;
+  Affine<V> x = total;
 #pragma unroll
   for (int off = 1; off < kWarp; off <<= 1) {
-    const Affine<R> y = shfl_up_affine(x, off);
+    const Affine<V> y = shfl_up_affine(x, off);
     if (lane >= off) x = compose(y, x);
   }
-  Affine<R> excl = shfl_up_affine(x, 1);
-  if (lane == 0) excl = affine_identity<R>();
+  Affine<V> excl = shfl_up_affine(x, 1);
+  if (lane == 0) excl = affine_identity<V>();
   if (nwarps > 1) {
     if (lane == kWarp - 1) warp_totals[warp] = x;
     __syncthreads();
     if (warp > 0) {
-      Affine<R> carry = warp_totals[0];
+      Affine<V> carry = warp_totals[0];
       for (int w = 1; w < warp; ++w) carry = compose(carry, warp_totals[w]);
       excl = compose(carry, excl);
     }
@@ -274,27 +381,27 @@ __device__ __forceinline__ Affine<R> cta_exclusive_affine(const Affine<R>& total
   return excl;
 }
 
-// Exclusive suffix sum over the CTA's threads of an N-word additive payload (sum over all higher
-// threads), warp level with shfl_down, CTA level through shared memory.
-template <typename R, int Words>
-__device__ __forceinline__ void cta_exclusive_suffix(const R (&val)[Words], R (&out)[Words], R* warp_sums, int nwarps) {
+// Exclusive suffix sum over the CTA's threads of a `Words`-word additive payload (sum over all
+// higher threads), warp level with shfl_down, CTA level through shared memory.
+template <typename V, int Words>
+__device__ __forceinline__ void cta_exclusive_suffix(const V (&val)[Words], V (&out)[Words], V* warp_sums, int nwarps) {
   const int lane = threadIdx.x & (kWarp - 1);
   const int warp = threadIdx.x / kWarp;
-  R x[Words];
+  V x[Words];
 #pragma unroll
   for (int i = 0; i < Words; ++i) x[i] = val[i];
 #pragma unroll
   for (int off = 1; off < kWarp; off <<= 1) {
 #pragma unroll
     for (int i = 0; i < Words; ++i) {
-      const R y = shfl_down_r(x[i], off);
-      if (lane + off < kWarp) x[i] += y;
+      const V y = shfl_down(x[i], off);
+      if (lane + off < kWarp) x[i] = vadd(x[i], y);
     }
   }
 #pragma unroll
   for (int i = 0; i < Words; ++i) {
-    const R y = shfl_down_r(x[i], 1);
-    out[i] = (lane == kWarp - 1) ? R(0) : y;
+    const V y = shfl_down(x[i], 1);
+    out[i] = (lane == kWarp - 1) ? splat<V>(0) : y;
   }
   if (nwarps > 1) {
     if (lane == 0) {
@@ -304,113 +411,146 @@ __device__ __forceinline__ void cta_exclusive_suffix(const R (&val)[Words], R (&
     __syncthreads();
     for (int w = warp + 1; w < nwarps; ++w) {
 #pragma unroll
-      for (int i = 0; i < Words; ++i) out[i] += warp_sums[w * Words + i];
+      for (int i = 0; i < Words; ++i) out[i] = vadd(out[i], warp_sums[w * Words + i]);
     }
   }
 }
 
 // Sum over the CTA of one value per thread; the result is valid in thread 0.
-template <typename R>
-__device__ __forceinline__ R cta_sum_to_thread0(R x, R* warp_sums, int nwarps) {
+template <typename V>
+__device__ __forceinline__ V cta_sum_to_thread0(V x, V* warp_sums, int nwarps) {
 #pragma unroll
-  for (int off = kWarp / 2; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  for (int off = kWarp / 2; off > 0; off >>= 1) x = vadd(x, shfl_xor(x, off));
   if (nwarps > 1) {
     const int lane = threadIdx.x & (kWarp - 1);
     const int warp = threadIdx.x / kWarp;
     if (lane == 0) warp_sums[warp] = x;
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int w = 1; w < nwarps; ++w) x += warp_sums[w];
+      for (int w = 1; w < nwarps; ++w) x = vadd(x, warp_sums[w]);
     }
   }
   return x;
 }
 
 // ------------------------------------------------------------------------------------------
-// first frame of a chain (block.cu:113-148), computed in R by every thread
+// vector helpers
 // ------------------------------------------------------------------------------------------
-template <typename R>
-struct FirstFrame {
-  R p0[3], p1[3], p2[3];
-  R dir0[3], turn0[3], dir1[3], normal[3];
-  R F[9];  // row-major; columns are dir1, side = normal x dir1, normal
-  R s0, c0;
-};
-
-template <typename R>
-__device__ __forceinline__ R dot3(const R* a, const R* b) {
-  return a[0] * b[0] + a[1] * b[1] + a[2] * b[2];
+template <typename V>
+__device__ __forceinline__ V dot3(const V* a, const V* b) {
+  return vfma(a[2], b[2], vfma(a[1], b[1], vmul(a[0], b[0])));
 }
 
-template <typename R>
-__device__ __forceinline__ void cross3(const R* a, const R* b, R* out) {
-  const R x = a[1] * b[2] - a[2] * b[1];
-  const R y = a[2] * b[0] - a[0] * b[2];
-  const R z = a[0] * b[1] - a[1] * b[0];
+// a x b
+template <typename V>
+__device__ __forceinline__ void cross3(const V* a, const V* b, V* out) {
+  const V x = vfma(a[1], b[2], vneg(vmul(a[2], b[1])));
+  const V y = vfma(a[2], b[0], vneg(vmul(a[0], b[2])));
+  const V z = vfma(a[0], b[1], vneg(vmul(a[1], b[0])));
   out[0] = x;
   out[1] = y;
   out[2] = z;
 }
 
-// v / sqrt(max(|v|^2, eps)), eps = the float literal 1e-12f (frame_utils.cuh:7, 17-20)
-template <typename R>
-__device__ __forceinline__ void normalize3(R* v) {
-  const R n2 = dot3(v, v);
-  const R inv = R(1) / sqrt_r(max_r(n2, static_cast<R>(1.0e-12f)));
+// ------------------------------------------------------------------------------------------
+// first frame of a chain (block.cu:113-148)
+// ------------------------------------------------------------------------------------------
+// Anchor part, shared by every chain of a call: dir0 = normalized(first_direction) and
+// turn0 = normalized(n0 x dir0) with n0 the initial normal made perpendicular to dir0 (or
+// stable_perpendicular(dir0) when that vanishes, frame_utils.cuh:22-31).
+template <typename S>
+struct AnchorFrame {
+  S p0[3], dir0[3], turn0[3];
+};
+
+template <typename S>
+__device__ __forceinline__ void normalize3_s(S* v) {
+  const S n2 = v[0] * v[0] + v[1] * v[1] + v[2] * v[2];
+  const S inv = S(1) / sqrt(n2 > static_cast<S>(1.0e-12f) ? n2 : static_cast<S>(1.0e-12f));
   v[0] *= inv;
   v[1] *= inv;
   v[2] *= inv;
 }
 
-template <typename R, typename T>
-__device__ __forceinline__ void load_anchor(const T* p, R d0, R d1, R d2, R* out) {
-  if (p == nullptr) {
-    out[0] = d0;
-    out[1] = d1;
-    out[2] = d2;
-  } else {
-    out[0] = to_r<R>(p[0]);
-    out[1] = to_r<R>(p[1]);
-    out[2] = to_r<R>(p[2]);
-  }
+template <typename S>
+__device__ __forceinline__ void cross3_s(const S* a, const S* b, S* out) {
+  const S x = a[1] * b[2] - a[2] * b[1];
+  const S y = a[2] * b[0] - a[0] * b[2];
+  const S z = a[0] * b[1] - a[1] * b[0];
+  out[0] = x;
+  out[1] = y;
+  out[2] = z;
 }
 
 // Anchors may be null: the reference's defaults (0,0,0), (1,0,0), (0,0,1) (reconstruct.py:69-71).
-template <typename R, typename T>
-__device__ __forceinline__ FirstFrame<R> first_frame(R l0, R l1, R a0, const T* p0, const T* first_direction, const T* initial_normal) {
-  FirstFrame<R> f;
-  load_anchor<R>(p0, R(0), R(0), R(0), f.p0);
-  load_anchor<R>(first_direction, R(1), R(0), R(0), f.dir0);
-  normalize3(f.dir0);
+template <typename S, typename T>
+__device__ __forceinline__ AnchorFrame<S> anchor_frame(const T* p0, const T* first_direction, const T* initial_normal) {
+  AnchorFrame<S> a;
+  if (p0 == nullptr && first_direction == nullptr && initial_normal == nullptr) {
+    // the general computation below gives exactly these values for the default anchors
 #pragma unroll
-  for (int i = 0; i < 3; ++i) f.p1[i] = f.p0[i] + l0 * f.dir0[i];
-  R n0[3];
-  load_anchor<R>(initial_normal, R(0), R(0), R(1), n0);
-  const R proj = dot3(n0, f.dir0);
-#pragma unroll
-  for (int i = 0; i < 3; ++i) n0[i] -= proj * f.dir0[i];
-  if (dot3(n0, n0) < static_cast<R>(1.0e-12f)) {
-    // stable_perpendicular (frame_utils.cuh:22-31)
-    R helper[3] = {R(1), R(0), R(0)};
-    if (abs_r(f.dir0[0]) >= static_cast<R>(0.9)) {
-      helper[0] = R(0);
-      helper[1] = R(1);
+    for (int i = 0; i < 3; ++i) {
+      a.p0[i] = S(0);
+      a.dir0[i] = S(i == 0);
+      a.turn0[i] = S(i == 1);
     }
-    cross3(f.dir0, helper, n0);
-    normalize3(n0);
-  } else {
-    normalize3(n0);
+    return a;
   }
-  cross3(n0, f.dir0, f.turn0);
-  normalize3(f.turn0);
-  sin_cos(a0, f.s0, f.c0);
+  S n0[3];
 #pragma unroll
-  for (int i = 0; i < 3; ++i) f.dir1[i] = -f.c0 * f.dir0[i] + f.s0 * f.turn0[i];
+  for (int i = 0; i < 3; ++i) {
+    a.p0[i] = p0 ? to_r<S>(p0[i]) : S(0);
+    a.dir0[i] = first_direction ? to_r<S>(first_direction[i]) : S(i == 0);
+    n0[i] = initial_normal ? to_r<S>(initial_normal[i]) : S(i == 2);
+  }
+  normalize3_s(a.dir0);
+  const S proj = n0[0] * a.dir0[0] + n0[1] * a.dir0[1] + n0[2] * a.dir0[2];
 #pragma unroll
-  for (int i = 0; i < 3; ++i) f.p2[i] = f.p1[i] + l1 * f.dir1[i];
-  cross3(f.dir0, f.dir1, f.normal);
-  normalize3(f.normal);
-  R side[3];
+  for (int i = 0; i < 3; ++i) n0[i] -= proj * a.dir0[i];
+  if (n0[0] * n0[0] + n0[1] * n0[1] + n0[2] * n0[2] < static_cast<S>(1.0e-12f)) {
+    S helper[3] = {S(1), S(0), S(0)};
+    if ((a.dir0[0] < S(0) ? -a.dir0[0] : a.dir0[0]) >= static_cast<S>(0.9)) {
+      helper[0] = S(0);
+      helper[1] = S(1);
+    }
+    cross3_s(a.dir0, helper, n0);
+  }
+  normalize3_s(n0);
+  cross3_s(n0, a.dir0, a.turn0);
+  normalize3_s(a.turn0);
+  return a;
+}
+
+// Chain part, per lane: p1, p2 and F = [dir1 | normal x dir1 | normal] (row-major).
+template <typename V>
+struct ChainFrame {
+  V p1[3], p2[3], dir1[3], normal[3];
+  V F[9];
+  V s0, c0;
+};
+
+template <typename V>
+__device__ __forceinline__ ChainFrame<V> chain_frame(const AnchorFrame<typename Lanes<V>::S>& a, V l0, V l1, V a0) {
+  ChainFrame<V> f;
+  V st, ct, sp, cp;
+  step_sincos(a0, a0, st, ct, sp, cp);
+  f.s0 = st;
+  f.c0 = ct;
+  V dir0[3], turn0[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    dir0[i] = splat<V>(a.dir0[i]);
+    turn0[i] = splat<V>(a.turn0[i]);
+    f.p1[i] = vfma(l0, dir0[i], splat<V>(a.p0[i]));
+    f.dir1[i] = vfma(st, turn0[i], vmul(vneg(ct), dir0[i]));
+  }
+#pragma unroll
+  for (int i = 0; i < 3; ++i) f.p2[i] = vfma(l1, f.dir1[i], f.p1[i]);
+  cross3(dir0, f.dir1, f.normal);
+  const V inv = vrecip_sqrt_clamped(dot3(f.normal, f.normal));
+#pragma unroll
+  for (int i = 0; i < 3; ++i) f.normal[i] = vmul(f.normal[i], inv);
+  V side[3];
   cross3(f.normal, f.dir1, side);
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
@@ -425,6 +565,7 @@ __device__ __forceinline__ FirstFrame<R> first_frame(R l0, R l1, R a0, const T* 
 // launch geometry shared by host and device
 // ------------------------------------------------------------------------------------------
 struct ChainGeometry {
+  int batch;   // B
   int points;  // N
   int steps;   // N - 3
   int items;   // K: steps per thread (odd)

@@ -80,4 +80,40 @@ CUFKB_HD void sincos_fast(float x, float& s, float& c) {
   c = u2f(f2u(cc) ^ (((quadrant + 1u) & 2u) << 30));
 }
 
+#if defined(__CUDACC__)
+// The same computation on two independent arguments with Blackwell's packed FP32 instructions
+// (fma/mul/add .f32x2): every multiply-add above becomes one instruction for both lanes, and each
+// lane's result is bit-identical to sincos_fast on that lane.  Device code for sm_100 and later.
+__device__ __forceinline__ void sincos_fast2(float2 x, float2& s, float2& c) {
+  const float2 two_over_pi = make_float2(0.6366197466850281f, 0.6366197466850281f);
+  const float2 shifter = make_float2(12582912.0f, 12582912.0f);
+  const float2 neg_shifter = make_float2(-12582912.0f, -12582912.0f);
+  const float2 neg_hi = make_float2(-1.57080078125f, -1.57080078125f);
+  const float2 neg_mid = make_float2(4.453584551811218e-06f, 4.453584551811218e-06f);
+  const float2 neg_lo = make_float2(8.705515752716053e-10f, 8.705515752716053e-10f);
+  const float2 t = __ffma2_rn(x, two_over_pi, shifter);
+  const float2 k = __fadd2_rn(t, neg_shifter);
+  float2 r = __ffma2_rn(k, neg_hi, x);
+  r = __ffma2_rn(k, neg_mid, r);
+  r = __ffma2_rn(k, neg_lo, r);
+  const float2 r2 = __fmul2_rn(r, r);
+  float2 p = make_float2(2.7557318844628753e-06f, 2.7557318844628753e-06f);
+  p = __ffma2_rn(p, r2, make_float2(-0.00019841270113829523f, -0.00019841270113829523f));
+  p = __ffma2_rn(p, r2, make_float2(0.008333333767950535f, 0.008333333767950535f));
+  p = __ffma2_rn(p, r2, make_float2(-0.1666666716337204f, -0.1666666716337204f));
+  const float2 sr = __ffma2_rn(p, __fmul2_rn(r, r2), r);
+  float2 q = make_float2(-2.755731998149713e-07f, -2.755731998149713e-07f);
+  q = __ffma2_rn(q, r2, make_float2(2.4801587642286904e-05f, 2.4801587642286904e-05f));
+  q = __ffma2_rn(q, r2, make_float2(-0.0013888889225199819f, -0.0013888889225199819f));
+  q = __ffma2_rn(q, r2, make_float2(0.0416666679084301f, 0.0416666679084301f));
+  q = __ffma2_rn(q, r2, make_float2(-0.5f, -0.5f));
+  const float2 cr = __ffma2_rn(q, r2, make_float2(1.0f, 1.0f));
+  const uint32_t qx = f2u(t.x), qy = f2u(t.y);
+  const float sx = (qx & 1u) ? cr.x : sr.x, cx = (qx & 1u) ? sr.x : cr.x;
+  const float sy = (qy & 1u) ? cr.y : sr.y, cy = (qy & 1u) ? sr.y : cr.y;
+  s = make_float2(u2f(f2u(sx) ^ ((qx & 2u) << 30)), u2f(f2u(sy) ^ ((qy & 2u) << 30)));
+  c = make_float2(u2f(f2u(cx) ^ (((qx + 1u) & 2u) << 30)), u2f(f2u(cy) ^ (((qy + 1u) & 2u) << 30)));
+}
+#endif
+
 }  // namespace cufkb
