@@ -10,6 +10,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <initializer_list>
 #include <mutex>
 
 namespace {
@@ -19,11 +20,11 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 32;
+constexpr int kNumKernels = 20;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 #ifndef CUFKB_TARGET_WARPS_PER_SM
-#define CUFKB_TARGET_WARPS_PER_SM 20
+#define CUFKB_TARGET_WARPS_PER_SM 32
 #endif
 constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;  // resident warps per SM the plan aims for
 
@@ -204,23 +205,6 @@ int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int 
   return CUFKB_SUCCESS;
 }
 
-// Chains per CTA: two float chains share a CTA (float2 lanes, packed f32x2 arithmetic) when the
-// batch still gives every SM several CTAs; float64 and small batches use one chain per CTA.
-#ifndef CUFKB_PAIR_MIN_CTAS_PER_SM
-#define CUFKB_PAIR_MIN_CTAS_PER_SM 4
-#endif
-template <typename T>
-bool use_pairs(int64_t batch, const DeviceCache& d) {
-  if constexpr (std::is_same_v<T, double>) {
-    return false;
-  } else {
-    return batch / 2 >= int64_t(d.sm_count) * CUFKB_PAIR_MIN_CTAS_PER_SM;
-  }
-}
-
-// Kernel ids for the caches: kind (4) x dtype (4) x chains per CTA (2).
-constexpr int kernel_id(int kind, int dtype, int chains) { return (kind * 4 + dtype) * 2 + (chains - 1); }
-
 template <typename T>
 constexpr int dtype_index() {
   if constexpr (std::is_same_v<T, float>) return 0;
@@ -229,36 +213,83 @@ constexpr int dtype_index() {
   return 3;
 }
 
-template <typename T, int kC>
-int block_forward_launch(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
-                         int points, cudaStream_t stream) {
-  const size_t smem = kC * cufkb::block_region_bytes<T>(points, false);
-  auto kernel = cufkb::block_forward_kernel<T, kC>;
-  const int64_t ctas = (batch + kC - 1) / kC;
+// Kernel ids for the caches: kind (5) x dtype (4).
+enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardSaved = 4 };
+constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
+
+template <typename T>
+using StateT = typename cufkb::ComputeOf<T>::type;
+
+// The forward's plan: the saved-state backward must use the same threads per chain and steps per
+// thread, so both compute it from the forward kernel's footprint.
+template <typename T>
+int block_forward_plan(int64_t batch, int points, LaunchEnv* env, size_t* smem) {
+  *smem = cufkb::block_smem_bytes<T>(points, false);
+  return launch_env(env, cufkb::block_forward_kernel<T>, kernel_id(kBlockForward, dtype_index<T>()), batch, points, *smem);
+}
+
+template <typename T>
+int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, void* state, int64_t batch,
+                       int points, cudaStream_t stream) {
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(0, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  size_t smem;
+  if (int st = block_forward_plan<T>(batch, points, &env, &smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
+  cufkb::block_forward_kernel<T><<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz),
+                                                                                                   static_cast<StateT<T>*>(state), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
-template <typename T, int kC>
-int block_backward_launch(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL,
-                          void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
-  const size_t smem = kC * cufkb::block_region_bytes<T>(points, true);
-  auto kernel = cufkb::block_backward_kernel<T, kC>;
-  const int64_t ctas = (batch + kC - 1) / kC;
+template <typename T>
+int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL, void* gA,
+                        void* gD, int64_t batch, int points, cudaStream_t stream) {
+  const size_t smem = cufkb::block_smem_bytes<T>(points, true);
+  auto kernel = cufkb::block_backward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(1, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackward, dtype_index<T>()), batch, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
                                                                           static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Saved-state backward (32- and 64-bit types): the forward's plan, its xyz and its state.
+template <typename T>
+int block_backward_saved_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz,
+                              const void* state, const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
+  LaunchEnv fwd;
+  size_t fwd_smem;
+  if (int st = block_forward_plan<T>(batch, points, &fwd, &fwd_smem)) return st;
+  const size_t smem = cufkb::block_smem_bytes<T>(points, true);
+  auto kernel = cufkb::block_backward_saved_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardSaved, dtype_index<T>()), batch, points, smem)) return st;
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, fwd.plan.items};
+  kernel<<<static_cast<unsigned>(batch), fwd.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const StateT<T>*>(state),
+                                                                         static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
+                                                                         static_cast<T*>(gD), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int block_state_bytes(int64_t batch, int points, size_t* bytes) {
+  *bytes = 0;
+  if constexpr (sizeof(T) >= 4) {
+    if (batch == 0) return CUFKB_SUCCESS;
+    LaunchEnv env;
+    size_t smem;
+    if (int st = block_forward_plan<T>(batch, points, &env, &smem)) return st;
+    *bytes = static_cast<size_t>(batch) * env.plan.threads * cufkb::kStateWords * sizeof(StateT<T>);
+  }
   return CUFKB_SUCCESS;
 }
 
@@ -273,93 +304,66 @@ cufkb::TorsionConsts<R> torsion_consts(const cufkb_torsion_constants* c) {
   return out;
 }
 
-template <typename T, int kC>
-int torsion_forward_launch(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
-                           cudaStream_t stream) {
+template <typename T>
+int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
-  const size_t smem = kC * cufkb::torsion_region_bytes<T>(points, false);
-  auto kernel = cufkb::torsion_forward_kernel<T, kC>;
-  const int64_t ctas = (batch + kC - 1) / kC;
+  const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
+  auto kernel = cufkb::torsion_forward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(2, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionForward, dtype_index<T>()), batch, points, smem)) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
-                                                                          static_cast<T*>(xyz), geo);
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c), static_cast<T*>(xyz),
+                                                                          geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
-template <typename T, int kC>
-int torsion_backward_launch(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw, int64_t grad_stride,
-                            int64_t batch, int points, cudaStream_t stream) {
+template <typename T>
+int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw, int64_t grad_stride,
+                          int64_t batch, int points, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
-  const size_t smem = kC * cufkb::torsion_region_bytes<T>(points, true);
-  auto kernel = cufkb::torsion_backward_kernel<T, kC>;
-  const int64_t ctas = (batch + kC - 1) / kC;
+  const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
+  auto kernel = cufkb::torsion_backward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(3, dtype_index<T>(), kC), ctas, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackward, dtype_index<T>()), batch, points, smem)) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(ctas), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                           static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
-// Dispatch on chains per CTA (needs the device attributes, hence the current-device lookup).
-template <typename T, typename Fn1, typename Fn2>
-int with_pairs(int64_t batch, Fn1 single, Fn2 pair) {
-  int dev = 0;
-  if (int e = current_device(&dev)) return fail_cuda(static_cast<cudaError_t>(e));
-  const DeviceCache* d = device_cache(dev);
-  if (d->error != 0) return fail_cuda(static_cast<cudaError_t>(d->error));
-  return use_pairs<T>(batch, *d) ? pair() : single();
-}
+}  // namespace
 
-template <typename T>
-int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
-                       int points, cudaStream_t s) {
-  if constexpr (std::is_same_v<T, double>) {
-    return block_forward_launch<T, 1>(L, A, D, p0, fd, nn, xyz, batch, points, s);
-  } else {
-    return with_pairs<T>(
-        batch, [&] { return block_forward_launch<T, 1>(L, A, D, p0, fd, nn, xyz, batch, points, s); },
-        [&] { return block_forward_launch<T, 2>(L, A, D, p0, fd, nn, xyz, batch, points, s); });
+namespace {
+
+int check_block_pointers(int dtype, std::initializer_list<const void*> required, std::initializer_list<const void*> all) {
+  for (const void* p : required) {
+    if (!p) return CUFKB_ERROR_NULL_POINTER;
   }
-}
-
-template <typename T>
-int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL,
-                        void* gA, void* gD, int64_t batch, int points, cudaStream_t s) {
-  if constexpr (std::is_same_v<T, double>) {
-    return block_backward_launch<T, 1>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s);
-  } else {
-    return with_pairs<T>(
-        batch, [&] { return block_backward_launch<T, 1>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s); },
-        [&] { return block_backward_launch<T, 2>(L, A, D, p0, fd, nn, g, gL, gA, gD, batch, points, s); });
+  const size_t es = elem_size(dtype);
+  for (const void* p : all) {
+    if (!aligned(p, es)) return CUFKB_ERROR_MISALIGNED;
   }
+  return CUFKB_SUCCESS;
 }
 
-template <typename T>
-int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points,
-                         cudaStream_t s) {
-  if constexpr (std::is_same_v<T, double>) {
-    return torsion_forward_launch<T, 1>(raw, raw_stride, c, xyz, batch, points, s);
-  } else {
-    return with_pairs<T>(
-        batch, [&] { return torsion_forward_launch<T, 1>(raw, raw_stride, c, xyz, batch, points, s); },
-        [&] { return torsion_forward_launch<T, 2>(raw, raw_stride, c, xyz, batch, points, s); });
-  }
-}
-
-template <typename T>
-int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* g, void* graw, int64_t grad_stride,
-                          int64_t batch, int points, cudaStream_t s) {
-  if constexpr (std::is_same_v<T, double>) {
-    return torsion_backward_launch<T, 1>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s);
-  } else {
-    return with_pairs<T>(
-        batch, [&] { return torsion_backward_launch<T, 1>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s); },
-        [&] { return torsion_backward_launch<T, 2>(raw, raw_stride, c, g, graw, grad_stride, batch, points, s); });
+int block_forward_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, void* state,
+                           int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {L, A, D, xyz}, {L, A, D, p0, fd, nn, xyz})) return st;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, state, batch, n, s);
+    case CUFKB_FLOAT64:
+      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, state, batch, n, s);
+    case CUFKB_FLOAT16:
+      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, nullptr, batch, n, s);
+    default:
+      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, nullptr, batch, n, s);
   }
 }
 
@@ -369,57 +373,84 @@ extern "C" {
 
 int cufkb_max_point_count(void) { return CUFKB_MAX_POINT_COUNT; }
 
-int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
-                        const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
-                        cufkb_stream_t stream) {
+int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                        const void* initial_normal, void* xyz, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, nullptr, batch, points, stream);
+}
+
+int cufkb_block_state_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes) {
+  if (!bytes) return CUFKB_ERROR_NULL_POINTER;
+  *bytes = 0;
   if (int st = check_shape(dtype, batch, points)) return st;
-  if (batch == 0) return CUFKB_SUCCESS;
-  if (!lengths || !angles || !dihedrals || !xyz) return CUFKB_ERROR_NULL_POINTER;
-  const size_t es = elem_size(dtype);
-  for (const void* p : {lengths, angles, dihedrals, p0, first_direction, initial_normal, static_cast<const void*>(xyz)}) {
-    if (!aligned(p, es)) return CUFKB_ERROR_MISALIGNED;
-  }
   const int n = static_cast<int>(points);
-  auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_forward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
+      return block_state_bytes<float>(batch, n, bytes);
     case CUFKB_FLOAT64:
-      return block_forward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
-    case CUFKB_FLOAT16:
-      return block_forward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
+      return block_state_bytes<double>(batch, n, bytes);
     default:
-      return block_forward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, n, s);
+      return CUFKB_SUCCESS;
   }
 }
 
-int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
-                         const void* first_direction, const void* initial_normal, const void* grad_xyz, void* grad_lengths,
-                         void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
+int cufkb_block_forward_save(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                             const void* initial_normal, void* xyz, void* state, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if ((dtype == CUFKB_FLOAT32 || dtype == CUFKB_FLOAT64) && batch > 0 && state == nullptr) return CUFKB_ERROR_NULL_POINTER;
+  if (!aligned(state, 16)) return CUFKB_ERROR_MISALIGNED;
+  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, batch, points, stream);
+}
+
+int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                         const void* initial_normal, const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                         int64_t points, cufkb_stream_t stream) {
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
-  if (!lengths || !angles || !dihedrals || !grad_xyz || !grad_lengths || !grad_angles || !grad_dihedrals) return CUFKB_ERROR_NULL_POINTER;
-  const size_t es = elem_size(dtype);
-  for (const void* p : {lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, static_cast<const void*>(grad_lengths),
-                        static_cast<const void*>(grad_angles), static_cast<const void*>(grad_dihedrals)}) {
-    if (!aligned(p, es)) return CUFKB_ERROR_MISALIGNED;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
   }
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                        grad_angles, grad_dihedrals, batch, n, s);
+      return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                        grad_dihedrals, batch, n, s);
     case CUFKB_FLOAT64:
-      return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                         grad_angles, grad_dihedrals, batch, n, s);
+      return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s);
     case CUFKB_FLOAT16:
-      return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths,
-                                         grad_angles, grad_dihedrals, batch, n, s);
+      return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s);
     default:
-      return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz,
-                                                grad_lengths, grad_angles, grad_dihedrals, batch, n, s);
+      return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                                grad_dihedrals, batch, n, s);
   }
+}
+
+int cufkb_block_backward_saved(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                               const void* initial_normal, const void* xyz, const void* state, const void* grad_xyz, void* grad_lengths,
+                               void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
+    return cufkb_block_backward(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                grad_dihedrals, batch, points, stream);
+  }
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, state, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
+  }
+  if (!aligned(state, 16)) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    return block_backward_saved_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, grad_xyz, grad_lengths,
+                                            grad_angles, grad_dihedrals, batch, n, s);
+  }
+  return block_backward_saved_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, grad_xyz, grad_lengths, grad_angles,
+                                           grad_dihedrals, batch, n, s);
 }
 
 int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,

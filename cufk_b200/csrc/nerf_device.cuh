@@ -1,18 +1,18 @@
 // Device-side building blocks of the sm_100a NeRF chain kernels.
 //
 // Layout conventions used by every kernel in this library:
-//   * one CTA reconstructs C = 1 or 2 chains; its W warps own consecutive runs of K steps per lane
-//     (thread t owns steps [t*K, t*K + K) of every chain of the CTA), K odd so that the lanes'
-//     shared-memory strides (3K words) hit 32 distinct banks;
+//   * one CTA reconstructs one chain; its W warps own consecutive runs of K steps per lane
+//     (thread t owns steps [t*K, t*K + K)), K odd so that the lanes' shared-memory strides (3K words)
+//     hit 32 distinct banks;
 //   * a chain's per-atom data lives in shared memory as "slots": atom a owns the three words
 //     X[3a..3a+2].  Inputs are scattered into the slot of the atom they place (length L[i] ->
 //     X[3(i+1)], angle A[i] -> X[3(i+2)+1], dihedral D[i] -> X[3(i+3)+2]), so that step s reads
 //     its (L[s+2], A[s+1], D[s]) from slot s+3 and can overwrite it in place with its result:
 //     the xyz of atom s+3 in the forward, the three parameter gradients in the backward.  The slot
 //     array then has exactly the layout of the (N, 3) output row;
-//   * arithmetic runs on a lane type V: float (one float chain per CTA), float2 (two float chains
-//     per CTA, chain 0 in .x and chain 1 in .y, so that every multiply-add is one packed sm_100
-//     f32x2 instruction for both chains) or double.
+//   * arithmetic runs on the compute type V (float for 32- and 16-bit storage, double for float64)
+//     through explicit multiply-adds; the two angles of a step share one packed sm_100 f32x2
+//     evaluation of their sine/cosine polynomials.
 //
 // Reference behaviour restated here (paths relative to the cufk project root):
 //   * local transform R rows [(-c,-s,0), (sC,-cC,-S), (sS,-cS,C)], t = l R[:,0]
@@ -71,7 +71,7 @@ __device__ __forceinline__ T from_r(R x) {
 }
 
 // ------------------------------------------------------------------------------------------
-// lane arithmetic: V = float | float2 | double
+// arithmetic on the compute type V = float | double
 // ------------------------------------------------------------------------------------------
 template <typename V>
 struct Lanes;
@@ -81,11 +81,6 @@ struct Lanes<float> {
   static constexpr int kCount = 1;
 };
 template <>
-struct Lanes<float2> {
-  using S = float;
-  static constexpr int kCount = 2;
-};
-template <>
 struct Lanes<double> {
   using S = double;
   static constexpr int kCount = 1;
@@ -93,61 +88,40 @@ struct Lanes<double> {
 
 __device__ __forceinline__ float vfma(float a, float b, float c) { return fmaf(a, b, c); }
 __device__ __forceinline__ double vfma(double a, double b, double c) { return fma(a, b, c); }
-__device__ __forceinline__ float2 vfma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float vmul(float a, float b) { return a * b; }
 __device__ __forceinline__ double vmul(double a, double b) { return a * b; }
-__device__ __forceinline__ float2 vmul(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float vadd(float a, float b) { return a + b; }
 __device__ __forceinline__ double vadd(double a, double b) { return a + b; }
-__device__ __forceinline__ float2 vadd(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float vneg(float a) { return -a; }
 __device__ __forceinline__ double vneg(double a) { return -a; }
-__device__ __forceinline__ float2 vneg(float2 a) { return make_float2(-a.x, -a.y); }
 // a - b
 __device__ __forceinline__ float vsub(float a, float b) { return a - b; }
 __device__ __forceinline__ double vsub(double a, double b) { return a - b; }
-__device__ __forceinline__ float2 vsub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
 
 template <typename V>
 __device__ __forceinline__ V splat(typename Lanes<V>::S x) {
-  if constexpr (std::is_same_v<V, float2>) {
-    return make_float2(x, x);
-  } else {
-    return x;
-  }
+  return x;
 }
 
-template <typename V>
-__device__ __forceinline__ typename Lanes<V>::S lane(const V& v, int i) {
-  if constexpr (std::is_same_v<V, float2>) {
-    return i == 0 ? v.x : v.y;
-  } else {
-    return v;
-  }
-}
-
-// per-lane helpers for the rare non-multiply-add operations
-template <typename V, typename Fn>
-__device__ __forceinline__ V lanewise(const V& a, Fn fn) {
-  if constexpr (std::is_same_v<V, float2>) {
-    return make_float2(fn(a.x), fn(a.y));
-  } else {
-    return fn(a);
-  }
-}
-
+// 1 / sqrt(max(n2, 1e-12f)) (the clamp of normalized, frame_utils.cuh:17-20)
 template <typename V>
 __device__ __forceinline__ V vrecip_sqrt_clamped(V n2) {
-  return lanewise(n2, [](auto x) {
-    using S = decltype(x);
-    return S(1) / sqrt(x > static_cast<S>(1.0e-12f) ? x : static_cast<S>(1.0e-12f));
-  });
+  return V(1) / sqrt(n2 > static_cast<V>(1.0e-12f) ? n2 : static_cast<V>(1.0e-12f));
 }
 
 // sine and cosine of an angle pair (one step: bond angle and dihedral).  Float angles of real chains
 // take the packed short reduction of nerf_math.cuh; anything beyond its range (or NaN/inf) takes
 // the CUDA library routine for that step.  float64 always uses the library routine.
 __device__ __forceinline__ bool fast_range(float x) { return fabsf(x) <= kSinCosFastRange; }
+
+// Kept out of line: the library routine's large-argument reduction would otherwise sit inside every
+// unrolled step of the hot loops and crowd the instruction cache.
+__device__ __noinline__ float4 step_sincos_library(float th, float ph) {
+  float4 r;
+  sincosf(th, &r.x, &r.y);
+  sincosf(ph, &r.z, &r.w);
+  return r;
+}
 
 __device__ __forceinline__ void step_sincos(float th, float ph, float& st, float& ct, float& sp, float& cp) {
   if (fast_range(th) && fast_range(ph)) {
@@ -158,20 +132,11 @@ __device__ __forceinline__ void step_sincos(float th, float ph, float& st, float
     sp = s.y;
     cp = c.y;
   } else {
-    sincosf(th, &st, &ct);
-    sincosf(ph, &sp, &cp);
-  }
-}
-
-__device__ __forceinline__ void step_sincos(float2 th, float2 ph, float2& st, float2& ct, float2& sp, float2& cp) {
-  if (fast_range(th.x) && fast_range(th.y) && fast_range(ph.x) && fast_range(ph.y)) {
-    sincos_fast2(th, st, ct);
-    sincos_fast2(ph, sp, cp);
-  } else {
-    sincosf(th.x, &st.x, &ct.x);
-    sincosf(th.y, &st.y, &ct.y);
-    sincosf(ph.x, &sp.x, &cp.x);
-    sincosf(ph.y, &sp.y, &cp.y);
+    const float4 r = step_sincos_library(th, ph);
+    st = r.x;
+    ct = r.y;
+    sp = r.z;
+    cp = r.w;
   }
 }
 
@@ -309,8 +274,7 @@ __device__ __forceinline__ StepRot<V> step_rot(V l, V s, V c, V S, V C) {
 // P <- P * L(l, theta, phi) with L = (Rx(phi) Mz(theta), l Rx(phi) Mz(theta) e_x):
 //   Rx(phi) = [[1,0,0],[0,C,-S],[0,S,C]],  Mz(theta) = [[-c,-s,0],[s,-c,0],[0,0,1]].
 // Their product is the reference's local rotation; the translation is l times the new first
-// column, so one step costs 27 multiply-adds (one instruction per multiply-add for both chains
-// of a float2 lane pair).
+// column, so one step costs 27 multiply-adds.
 template <typename V>
 __device__ __forceinline__ void advance(Affine<V>& P, const StepRot<V>& q) {
 #pragma unroll
@@ -331,19 +295,10 @@ __device__ __forceinline__ void advance(Affine<V>& P, const StepRot<V>& q) {
 
 __device__ __forceinline__ float shfl_up(float x, int off) { return __shfl_up_sync(0xffffffffu, x, off); }
 __device__ __forceinline__ double shfl_up(double x, int off) { return __shfl_up_sync(0xffffffffu, x, off); }
-__device__ __forceinline__ float2 shfl_up(float2 x, int off) {
-  return make_float2(__shfl_up_sync(0xffffffffu, x.x, off), __shfl_up_sync(0xffffffffu, x.y, off));
-}
 __device__ __forceinline__ float shfl_down(float x, int off) { return __shfl_down_sync(0xffffffffu, x, off); }
 __device__ __forceinline__ double shfl_down(double x, int off) { return __shfl_down_sync(0xffffffffu, x, off); }
-__device__ __forceinline__ float2 shfl_down(float2 x, int off) {
-  return make_float2(__shfl_down_sync(0xffffffffu, x.x, off), __shfl_down_sync(0xffffffffu, x.y, off));
-}
 __device__ __forceinline__ float shfl_xor(float x, int m) { return __shfl_xor_sync(0xffffffffu, x, m); }
 __device__ __forceinline__ double shfl_xor(double x, int m) { return __shfl_xor_sync(0xffffffffu, x, m); }
-__device__ __forceinline__ float2 shfl_xor(float2 x, int m) {
-  return make_float2(__shfl_xor_sync(0xffffffffu, x.x, m), __shfl_xor_sync(0xffffffffu, x.y, m));
-}
 
 template <typename V>
 __device__ __forceinline__ Affine<V> shfl_up_affine(const Affine<V>& a, int off) {
@@ -521,7 +476,7 @@ __device__ __forceinline__ AnchorFrame<S> anchor_frame(const T* p0, const T* fir
   return a;
 }
 
-// Chain part, per lane: p1, p2 and F = [dir1 | normal x dir1 | normal] (row-major).
+// Chain part: p1, p2 and F = [dir1 | normal x dir1 | normal] (row-major).
 template <typename V>
 struct ChainFrame {
   V p1[3], p2[3], dir1[3], normal[3];
@@ -570,5 +525,9 @@ struct ChainGeometry {
   int steps;   // N - 3
   int items;   // K: steps per thread (odd)
 };
+
+// Saved state of one chain for the backward: the world frame (rotation row-major, then translation)
+// in front of each thread's first step, written by the forward that computed it.
+constexpr int kStateWords = 12;
 
 }  // namespace cufkb

@@ -1,33 +1,39 @@
 // sm_100a kernels for the cufk reconstruction path.
 //
-// block_forward_kernel    <- src/cufk/csrc/block.cu:157-204   (xyz from lengths/angles/dihedrals)
-// block_backward_kernel   <- src/cufk/csrc/block.cu:206-313   (d lengths/angles/dihedrals)
-// torsion_forward_kernel  <- src/cufk/csrc/torsion.cu:254-295 (xyz from raw (sin, cos) pairs)
-// torsion_backward_kernel <- src/cufk/csrc/torsion.cu:297-381 (d raw pairs)
+// block_forward_kernel          <- src/cufk/csrc/block.cu:157-204   (xyz from lengths/angles/dihedrals)
+// block_backward_kernel         <- src/cufk/csrc/block.cu:206-313   (d lengths/angles/dihedrals)
+// block_backward_saved_kernel      the same gradients from the forward's xyz and saved frames
+// torsion_forward_kernel        <- src/cufk/csrc/torsion.cu:254-295 (xyz from raw (sin, cos) pairs)
+// torsion_backward_kernel       <- src/cufk/csrc/torsion.cu:297-381 (d raw pairs)
 //
-// One CTA reconstructs kC chains (1, or 2 for float arithmetic: the two chains ride in the two
-// halves of float2 lanes, so each multiply-add is one packed f32x2 instruction for both), with
-// W = blockDim.x / 32 warps and K (odd) consecutive steps per thread.
+// One CTA reconstructs one chain with W = blockDim.x / 32 warps and K (odd) consecutive steps per
+// thread.
 //
-// Forward: stage the chains' inputs into atom slots (LDGSTS), sweep each thread's K steps
+// Forward: stage the chain's inputs into atom slots (LDGSTS), sweep each thread's K steps
 // sequentially from the identity (the local prefix position written back into the slot), exclusive
 // affine scan of the thread totals across the CTA, then x = p2 + F (C.v + C.m v) per slot in place
-// and one bulk (TMA-engine) store per (N, 3) row.
+// and one bulk (TMA-engine) store of the (N, 3) row.  On request each thread also writes its world
+// frame (p2, F) C to a small state buffer (12 words per K steps).
 //
-// Backward (one kernel, nothing saved from the forward): the gradient of every parameter of
-// step s follows from the force/moment suffix of the atoms it moves.  In base-frame coordinates
-// (x~ = P.v, g~ = F^T g, P_s = L_0...L_s):
-//   F_s = sum_{j >= s+3} g~_j,  M_s = sum_{j >= s+3} x~_j x g~_j,  tau_s = M_s - x~_{s+2} x F_s,
+// Backward: the gradient of every parameter of step s follows from the force/moment suffix of the
+// atoms it moves.  In world coordinates (P_s = (F, p2) L_0...L_s, x = P.v):
+//   F_s = sum_{j >= s+3} g_j,  M_s = sum_{j >= s+3} x_j x g_j,  tau_s = M_s - x_{s+2} x F_s,
 //   d dihedral[s]   =  P_{s-1}.col0 . tau_s   (rotation about the incoming bond)
 //   d angle[s+1]    = -P_s.col2     . tau_s   (rotation about the frame normal)
 //   d length[s+2]   =  P_s.col0     . F_s     (translation along the new bond)
-// which is the derivative of the reference's forward for any base frame F; the first-frame
-// terms (lengths[0..1], angles[0]) follow write_first_frame_param_grads (block.cu:206-228).
-// Sweep 1 builds each thread's local prefix, its sum of g~ and the 3x3 moment matrix
-// Q = sum p (x) g~ (p = local position), so that once the affine scan gives the thread's carry C
-// the thread's moment total is C.v x G + axial(C.m Q) without revisiting its steps.  An exclusive
-// suffix scan of (G, M) gives each thread the sums of all later threads; sweep 2 recomputes the
-// prefix from C, walks the running suffix down and writes the gradients into the slots in place.
+// valid when the base frame F is orthonormal; otherwise the same formulas run in base-frame
+// coordinates (x~ = P.v without (F, p2), g~ = F^T g), which is the derivative of the reference's
+// forward for any F.  The first-frame terms (lengths[0..1], angles[0]) follow
+// write_first_frame_param_grads (block.cu:206-228).
+//   * Recompute form (block_backward_kernel, nothing saved): sweep 1 builds each thread's local
+//     prefix, its sum of g and the 3x3 moment matrix Q = sum p (x) g (p = local position), so that
+//     once the affine scan gives the thread's carry C its moment total is C.v x G + axial(C.m Q).
+//   * Saved form (block_backward_saved_kernel): the thread sums of g and x x g come straight from
+//     the forward's xyz and the carry from the saved state, so the chain is walked once instead of
+//     twice.
+//   Either way an exclusive suffix scan of the thread sums gives each thread the sums of all later
+//   threads, and sweep 2 recomputes the prefix from the carry, walks the running suffix down and
+//   writes the gradients into the slots in place.
 #pragma once
 
 #include "nerf_device.cuh"
@@ -51,10 +57,6 @@ struct TorsionConsts {
   R cos_a[3];
 };
 
-// Lane type of a CTA handling kC chains of compute type R.
-template <typename R, int kC>
-using LaneOf = std::conditional_t<kC == 2, float2, R>;
-
 // Shared memory of one CTA beyond the dynamic slots: scan exchange between warps.
 template <typename V>
 struct CtaExchange {
@@ -64,15 +66,16 @@ struct CtaExchange {
 };
 
 // --------------------------------------------------------------------------------------------
-// shared-memory layout: one region per chain of the CTA
+// shared-memory layout of one chain
 // --------------------------------------------------------------------------------------------
 // 4- and 8-byte types ("scatter"): [X slots, 3N elements of T, offset so that X has the residue of
-//   the output row mod 16] [G staged grad row (backward)]
+//   the output row mod 16] [G staged grad row (backward)]; the saved backward stages the forward's
+//   xyz into the slot row before the inputs (see block_backward_saved_kernel)
 // 16-bit types: [X slots, 3N floats] [staged input rows (T)] [G staged grad row (backward)]
 __host__ __device__ inline size_t slot_bytes(int points, size_t elem) { return staged_row_bytes(size_t(3) * points, elem); }
 
 template <typename T>
-__host__ __device__ inline size_t block_region_bytes(int points, bool backward) {
+__host__ __device__ inline size_t block_smem_bytes(int points, bool backward) {
   using R = typename ComputeOf<T>::type;
   size_t bytes = slot_bytes(points, sizeof(R));
   if (sizeof(T) < 4) {
@@ -83,7 +86,7 @@ __host__ __device__ inline size_t block_region_bytes(int points, bool backward) 
 }
 
 template <typename T>
-__host__ __device__ inline size_t torsion_region_bytes(int points, bool backward) {
+__host__ __device__ inline size_t torsion_smem_bytes(int points, bool backward) {
   using R = typename ComputeOf<T>::type;
   size_t bytes = slot_bytes(points, sizeof(R));
   if (sizeof(T) < 4) bytes += staged_row_bytes(size_t(2) * (points - 3), sizeof(T));
@@ -103,58 +106,27 @@ __device__ __forceinline__ StepRange step_range(int tid, int K, int S) {
   return {first, left < 0 ? 0 : (left < K ? left : K)};
 }
 
-// Per-chain shared-memory views of one CTA.
-template <typename T, int kC>
+// Shared-memory views of one chain.
+template <typename T>
 struct ChainViews {
   using R = typename ComputeOf<T>::type;
-  using V = LaneOf<R, kC>;
-  R* X[kC];                   // atom slots
-  const T* row[kC][3];        // staged input rows of 16-bit types (lengths/angles/dihedrals or raw pairs)
-  T* G[kC];                   // staged gradient rows (backward)
+  R* X;               // atom slots
+  const T* row[3];    // staged input rows of 16-bit types (lengths/angles/dihedrals or raw pairs)
+  T* G;               // staged gradient row (backward)
+  const T* Y;         // staged xyz row of the forward (saved backward)
 
-  __device__ __forceinline__ V slot(int off) const {
-    if constexpr (kC == 2) {
-      return make_float2(X[0][off], X[1][off]);
-    } else {
-      return X[0][off];
-    }
-  }
-  __device__ __forceinline__ void set_slot(int off, V v) const {
-    if constexpr (kC == 2) {
-      X[0][off] = v.x;
-      X[1][off] = v.y;
-    } else {
-      X[0][off] = v;
-    }
-  }
-  __device__ __forceinline__ V staged(int which, int i) const {
-    if constexpr (kC == 2) {
-      return make_float2(to_r<float>(row[0][which][i]), to_r<float>(row[1][which][i]));
-    } else {
-      return to_r<R>(row[0][which][i]);
-    }
-  }
-  __device__ __forceinline__ V grad(int off) const {
-    if constexpr (kC == 2) {
-      return make_float2(to_r<float>(G[0][off]), to_r<float>(G[1][off]));
-    } else {
-      return to_r<R>(G[0][off]);
-    }
-  }
-  __device__ __forceinline__ void set_grad(int off, V v) const {
-    if constexpr (kC == 2) {
-      G[0][off] = v.x;
-      G[1][off] = v.y;
-    } else {
-      G[0][off] = v;
-    }
-  }
+  __device__ __forceinline__ R slot(int off) const { return X[off]; }
+  __device__ __forceinline__ void set_slot(int off, R v) const { X[off] = v; }
+  __device__ __forceinline__ R staged(int which, int i) const { return to_r<R>(row[which][i]); }
+  __device__ __forceinline__ R grad(int off) const { return to_r<R>(G[off]); }
+  __device__ __forceinline__ void set_grad(int off, R v) const { G[off] = from_r<T>(v); }
+  __device__ __forceinline__ R pos(int off) const { return to_r<R>(Y[off]); }
 };
 
 // Block path inputs of step s: (L[s+2], A[s+1], D[s]).
-template <typename T, int kC>
-__device__ __forceinline__ void block_step_inputs(const ChainViews<T, kC>& cv, int s, LaneOf<typename ComputeOf<T>::type, kC>& l,
-                                                  LaneOf<typename ComputeOf<T>::type, kC>& th, LaneOf<typename ComputeOf<T>::type, kC>& ph) {
+template <typename T>
+__device__ __forceinline__ void block_step_inputs(const ChainViews<T>& cv, int s, typename ComputeOf<T>::type& l, typename ComputeOf<T>::type& th,
+                                                  typename ComputeOf<T>::type& ph) {
   if constexpr (sizeof(T) >= 4) {
     l = cv.slot(3 * (s + 3));
     th = cv.slot(3 * (s + 3) + 1);
@@ -177,39 +149,80 @@ __device__ __forceinline__ void scatter_block_inputs(T* X, const T* Lr, const T*
     cp_async<sizeof(T)>(slot + 7, Ar + i);
     cp_async<sizeof(T)>(slot + 11, Dr + i);
   }
-  if (i < N - 1) cp_async<sizeof(T)>(X + 3 * i + 3, Lr + i);
-  if (i < N - 2) cp_async<sizeof(T)>(X + 3 * i + 7, Ar + i);
-  i += nthr;
+  // the last two lengths and the last angle (indices N-3 and N-2 fall to two different threads)
   if (i < N - 1) cp_async<sizeof(T)>(X + 3 * i + 3, Lr + i);
   if (i < N - 2) cp_async<sizeof(T)>(X + 3 * i + 7, Ar + i);
 }
 
-// x = p2 + F (C.v + C.m v) for every slot the thread owns (in place).
-template <typename T, int kC, typename V>
-__device__ __forceinline__ void apply_carry(const ChainViews<T, kC>& cv, const Affine<V>& carry, const V* F, const V* p2, StepRange r) {
-  V G[9];
-  V h[3];
+// Stages a chain's inputs: scattered into the slots (4/8-byte types) or as rows (16-bit types, whose
+// slots hold float results).  Returns the first free byte after the chain's input region.
+template <typename T>
+__device__ __forceinline__ unsigned char* stage_block_inputs(ChainViews<T>& cv, unsigned char* smem, const BlockArgs<T>& args, int64_t chain, int N,
+                                                             uintptr_t slot_residue, int tid, int nthr) {
+  using R = typename ComputeOf<T>::type;
+  const T* Lr = args.lengths + chain * (N - 1);
+  const T* Ar = args.angles + chain * (N - 2);
+  const T* Dr = args.dihedrals + chain * (N - 3);
+  cv.X = reinterpret_cast<R*>(smem + slot_residue);
+  unsigned char* p = smem + slot_bytes(N, sizeof(R));
+  if constexpr (sizeof(T) >= 4) {
+    scatter_block_inputs<T>(reinterpret_cast<T*>(cv.X), Lr, Ar, Dr, N, tid, nthr);
+  } else {
+    cv.row[0] = stage_row_async(p, Lr, N - 1, tid, nthr);
+    p += staged_row_bytes(N - 1, sizeof(T));
+    cv.row[1] = stage_row_async(p, Ar, N - 2, tid, nthr);
+    p += staged_row_bytes(N - 2, sizeof(T));
+    cv.row[2] = stage_row_async(p, Dr, N - 3, tid, nthr);
+    p += staged_row_bytes(N - 3, sizeof(T));
+  }
+  return p;
+}
+
+template <typename T>
+__device__ __forceinline__ void first_inputs(const ChainViews<T>& cv, typename ComputeOf<T>::type& l0, typename ComputeOf<T>::type& l1,
+                                             typename ComputeOf<T>::type& a0) {
+  if constexpr (sizeof(T) >= 4) {
+    l0 = cv.slot(3);
+    l1 = cv.slot(6);
+    a0 = cv.slot(7);
+  } else {
+    l0 = cv.staged(0, 0);
+    l1 = cv.staged(0, 1);
+    a0 = cv.staged(1, 0);
+  }
+}
+
+// World carry (F, p2) C: the frame in front of the thread's first step.
+template <typename V>
+__device__ __forceinline__ Affine<V> world_carry(const Affine<V>& carry, const V* F, const V* p2) {
+  Affine<V> w;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      G[3 * i + j] = vfma(F[3 * i + 2], carry.m[6 + j], vfma(F[3 * i + 1], carry.m[3 + j], vmul(F[3 * i + 0], carry.m[0 + j])));
+      w.m[3 * i + j] = vfma(F[3 * i + 2], carry.m[6 + j], vfma(F[3 * i + 1], carry.m[3 + j], vmul(F[3 * i + 0], carry.m[0 + j])));
     }
-    h[i] = vfma(F[3 * i + 2], carry.v[2], vfma(F[3 * i + 1], carry.v[1], vfma(F[3 * i + 0], carry.v[0], p2[i])));
+    w.v[i] = vfma(F[3 * i + 2], carry.v[2], vfma(F[3 * i + 1], carry.v[1], vfma(F[3 * i + 0], carry.v[0], p2[i])));
   }
+  return w;
+}
+
+// x = W.v + W.m v for every slot the thread owns (in place), W its world carry.
+template <typename T, typename V>
+__device__ __forceinline__ void apply_carry(const ChainViews<T>& cv, const Affine<V>& W, StepRange r) {
   int off = 3 * (r.first + 3);
 #pragma unroll 4
   for (int k = 0; k < r.count; ++k, off += 3) {
     const V v0 = cv.slot(off), v1 = cv.slot(off + 1), v2 = cv.slot(off + 2);
-    cv.set_slot(off + 0, vfma(G[2], v2, vfma(G[1], v1, vfma(G[0], v0, h[0]))));
-    cv.set_slot(off + 1, vfma(G[5], v2, vfma(G[4], v1, vfma(G[3], v0, h[1]))));
-    cv.set_slot(off + 2, vfma(G[8], v2, vfma(G[7], v1, vfma(G[6], v0, h[2]))));
+    cv.set_slot(off + 0, vfma(W.m[2], v2, vfma(W.m[1], v1, vfma(W.m[0], v0, W.v[0]))));
+    cv.set_slot(off + 1, vfma(W.m[5], v2, vfma(W.m[4], v1, vfma(W.m[3], v0, W.v[1]))));
+    cv.set_slot(off + 2, vfma(W.m[8], v2, vfma(W.m[7], v1, vfma(W.m[6], v0, W.v[2]))));
   }
 }
 
 // Sweep 1 of the forward: local prefix positions into the slots; returns the thread total.
-template <typename T, int kC, typename V, typename StepFn>
-__device__ __forceinline__ Affine<V> sweep_local_prefix(const ChainViews<T, kC>& cv, StepRange r, StepFn step) {
+template <typename T, typename V, typename StepFn>
+__device__ __forceinline__ Affine<V> sweep_local_prefix(const ChainViews<T>& cv, StepRange r, StepFn step) {
   Affine<V> P = affine_identity<V>();
   int off = 3 * (r.first + 3);
 #pragma unroll 4
@@ -222,6 +235,22 @@ __device__ __forceinline__ Affine<V> sweep_local_prefix(const ChainViews<T, kC>&
   return P;
 }
 
+// Writes the slot array (3N values in R) to the output row.  Scatter types hold final T values
+// with the row's residue mod 16, so the row leaves in one bulk store; 16-bit types convert.
+template <typename T, typename R>
+__device__ __forceinline__ void store_xyz_row(T* out, const R* X, int N, int tid, int nthr) {
+  if constexpr (sizeof(T) >= 4) {
+    fence_proxy_async_smem();
+    __syncthreads();
+    store_row_bulk<T>(out, reinterpret_cast<const T*>(X), 3 * N, tid, nthr, 0);
+    if (tid == 0) bulk_store_wait_read();
+  } else {
+    __syncthreads();
+#pragma unroll 4
+    for (int e = tid; e < 3 * N; e += nthr) out[e] = from_r<T>(X[e]);
+  }
+}
+
 // g~ = F^T g
 template <typename V>
 __device__ __forceinline__ void to_base(const V* F, V g0, V g1, V g2, V* out) {
@@ -230,50 +259,43 @@ __device__ __forceinline__ void to_base(const V* F, V g0, V g1, V g2, V* out) {
   out[2] = vfma(F[8], g2, vfma(F[5], g1, vmul(F[2], g0)));
 }
 
-// Sweep 1 of the backward: thread total of the prefix, of g~ and of Q = sum p (x) g~.  When the
-// staged gradient row is in the compute type, g~ replaces g in place for sweep 2.
-template <typename T, int kC, typename V, typename StepFn>
-__device__ __forceinline__ Affine<V> sweep_backward_totals(const ChainViews<T, kC>& cv, const V* F, StepRange r, StepFn step, V (&gsum)[3],
-                                                          V (&Q)[9]) {
+// Sweep 1 of the recompute backward: thread total of the local prefix, of g and of
+// Q = sum p (x) g.  In base coordinates (kWorld false) g is g~ = F^T g, stored back in place for
+// sweep 2 when the staged row is in the compute type.
+template <bool kWorld, typename T, typename V, typename StepFn>
+__device__ __forceinline__ Affine<V> sweep_backward_totals(const ChainViews<T>& cv, const V* F, StepRange r, StepFn step, V (&gsum)[3], V (&Q)[9]) {
   using R = typename ComputeOf<T>::type;
   Affine<V> P = affine_identity<V>();
 #pragma unroll
-  for (int i = 0; i < 3; ++i) gsum[i] = splat<V>(0);
+  for (int i = 0; i < 3; ++i) gsum[i] = V(0);
 #pragma unroll
-  for (int i = 0; i < 9; ++i) Q[i] = splat<V>(0);
+  for (int i = 0; i < 9; ++i) Q[i] = V(0);
   int off = 3 * (r.first + 3);
 #pragma unroll 2
   for (int k = 0; k < r.count; ++k, off += 3) {
     advance(P, step(r.first + k));
-    V gt[3];
-    to_base(F, cv.grad(off), cv.grad(off + 1), cv.grad(off + 2), gt);
-    if constexpr (std::is_same_v<T, R>) {
-      cv.set_grad(off, gt[0]);
-      cv.set_grad(off + 1, gt[1]);
-      cv.set_grad(off + 2, gt[2]);
+    V g[3];
+    if constexpr (kWorld) {
+      g[0] = cv.grad(off);
+      g[1] = cv.grad(off + 1);
+      g[2] = cv.grad(off + 2);
+    } else {
+      to_base(F, cv.grad(off), cv.grad(off + 1), cv.grad(off + 2), g);
+      if constexpr (std::is_same_v<T, R>) {
+        cv.set_grad(off, g[0]);
+        cv.set_grad(off + 1, g[1]);
+        cv.set_grad(off + 2, g[2]);
+      }
     }
 #pragma unroll
-    for (int c = 0; c < 3; ++c) gsum[c] = vadd(gsum[c], gt[c]);
+    for (int c = 0; c < 3; ++c) gsum[c] = vadd(gsum[c], g[c]);
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
 #pragma unroll
-      for (int c = 0; c < 3; ++c) Q[3 * d + c] = vfma(P.v[d], gt[c], Q[3 * d + c]);
+      for (int c = 0; c < 3; ++c) Q[3 * d + c] = vfma(P.v[d], g[c], Q[3 * d + c]);
     }
   }
   return P;
-}
-
-// g~ of the atom at slot offset `off` in sweep 2 (stored by sweep 1 for the compute type).
-template <typename T, int kC, typename V>
-__device__ __forceinline__ void base_grad(const ChainViews<T, kC>& cv, int off, const V* F, V* gt) {
-  using R = typename ComputeOf<T>::type;
-  if constexpr (std::is_same_v<T, R>) {
-    gt[0] = cv.grad(off);
-    gt[1] = cv.grad(off + 1);
-    gt[2] = cv.grad(off + 2);
-  } else {
-    to_base(F, cv.grad(off), cv.grad(off + 1), cv.grad(off + 2), gt);
-  }
 }
 
 // Thread's moment total from its carry: C.v x G + axial(C.m Q).
@@ -291,167 +313,30 @@ __device__ __forceinline__ void moment_total(const Affine<V>& C, const V (&gsum)
   M[2] = vadd(M[2], vsub(H[1], H[3]));
 }
 
-// Suffix sums (force, moment) over all atoms from this thread's first step on.
+// Suffix sums (force, moment) over all atoms from this thread's first step on, from the thread's own
+// sums (gsum, msum).
 template <typename V>
-__device__ __forceinline__ void suffix_base(const Affine<V>& carry, const V (&gsum)[3], const V (&Q)[9], CtaExchange<V>& ex, int nwarps, V* Fs,
-                                            V* Ms) {
-  V mlane[3];
-  moment_total<V>(carry, gsum, Q, mlane);
-  V mine[6] = {gsum[0], gsum[1], gsum[2], mlane[0], mlane[1], mlane[2]};
+__device__ __forceinline__ void suffix_base(const V (&gsum)[3], const V* msum, CtaExchange<V>& ex, int nwarps, V* Fs, V* Ms) {
+  V mine[6] = {gsum[0], gsum[1], gsum[2], msum[0], msum[1], msum[2]};
   V after[6];
   cta_exclusive_suffix<V, 6>(mine, after, ex.warp_sums, nwarps);
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
     Fs[i] = vadd(after[i], gsum[i]);
-    Ms[i] = vadd(after[3 + i], mlane[i]);
+    Ms[i] = vadd(after[3 + i], msum[i]);
   }
-}
-
-// Per-chain row pointers of this CTA: chain c of the CTA is blockIdx.x * kC + c; a missing last
-// chain (odd batch) aliases chain 0's rows for reading and writes nothing.
-template <int kC>
-__device__ __forceinline__ int64_t cta_chain(int c, int batch, bool& valid) {
-  const int64_t idx = int64_t(blockIdx.x) * kC + c;
-  valid = idx < batch;
-  return valid ? idx : int64_t(blockIdx.x) * kC;
-}
-
-// --------------------------------------------------------------------------------------------
-// block path
-// --------------------------------------------------------------------------------------------
-template <typename T, int kC>
-__global__ void __launch_bounds__(kMaxWarps* kWarp) block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo) {
-  using R = typename ComputeOf<T>::type;
-  using S = R;
-  using V = LaneOf<R, kC>;
-  constexpr bool kScatter = sizeof(T) >= 4;
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ CtaExchange<V> ex;
-
-  const int N = geo.points, St = geo.steps, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const size_t region = block_region_bytes<T>(N, false);
-  ChainViews<T, kC> cv;
-  T* out[kC];
-  bool valid[kC];
-#pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const int64_t chain = cta_chain<kC>(c, geo.batch, valid[c]);
-    const T* Lr = args.lengths + chain * (N - 1);
-    const T* Ar = args.angles + chain * (N - 2);
-    const T* Dr = args.dihedrals + chain * (N - 3);
-    out[c] = xyz + chain * 3 * N;
-    unsigned char* base = smem + c * region;
-    if constexpr (kScatter) {
-      cv.X[c] = reinterpret_cast<R*>(base + (reinterpret_cast<uintptr_t>(out[c]) & 15u));
-      scatter_block_inputs<T>(reinterpret_cast<T*>(cv.X[c]), Lr, Ar, Dr, N, tid, nthr);
-    } else {
-      cv.X[c] = reinterpret_cast<R*>(base);
-      unsigned char* p = base + slot_bytes(N, sizeof(R));
-      cv.row[c][0] = stage_row_async(p, Lr, N - 1, tid, nthr);
-      p += staged_row_bytes(N - 1, sizeof(T));
-      cv.row[c][1] = stage_row_async(p, Ar, N - 2, tid, nthr);
-      p += staged_row_bytes(N - 2, sizeof(T));
-      cv.row[c][2] = stage_row_async(p, Dr, N - 3, tid, nthr);
-    }
-  }
-  const AnchorFrame<S> af = anchor_frame<S>(args.p0, args.first_direction, args.initial_normal);
-  cp_async_wait_all();
-  __syncthreads();
-
-  V F[9], p2[3];
-  {
-    V l0, l1, a0;
-    if constexpr (kScatter) {
-      l0 = cv.slot(3);
-      l1 = cv.slot(6);
-      a0 = cv.slot(7);
-    } else {
-      l0 = cv.staged(0, 0);
-      l1 = cv.staged(0, 1);
-      a0 = cv.staged(1, 0);
-    }
-    const ChainFrame<V> ff = chain_frame<V>(af, l0, l1, a0);
-#pragma unroll
-    for (int i = 0; i < 9; ++i) F[i] = ff.F[i];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) p2[i] = ff.p2[i];
-    if constexpr (kScatter) __syncthreads();  // every thread has read l0, l1, a0 from atom slots 1, 2
-    if (tid == 0) {
-#pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        cv.set_slot(i, splat<V>(af.p0[i]));
-        cv.set_slot(3 + i, ff.p1[i]);
-        cv.set_slot(6 + i, ff.p2[i]);
-      }
-    }
-  }
-
-  auto step = [&](int s) {
-    V l, th, ph, st, ct, sp, cp;
-    block_step_inputs<T, kC>(cv, s, l, th, ph);
-    step_sincos(th, ph, st, ct, sp, cp);
-    return step_rot(l, st, ct, sp, cp);
-  };
-
-  const StepRange range = step_range(tid, K, St);
-  const Affine<V> total = sweep_local_prefix<T, kC, V>(cv, range, step);
-  const Affine<V> carry = cta_exclusive_affine<V>(total, ex.warp_totals, nwarps);
-  apply_carry<T, kC, V>(cv, carry, F, p2, range);
-
-  if constexpr (kScatter) {
-    fence_proxy_async_smem();
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      if (valid[c]) store_row_bulk<T>(out[c], reinterpret_cast<const T*>(cv.X[c]), 3 * N, tid, nthr, c);
-    }
-    if (tid < kC) bulk_store_wait_read();
-  } else {
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      if (!valid[c]) continue;
-#pragma unroll 4
-      for (int e = tid; e < 3 * N; e += nthr) out[c][e] = from_r<T>(cv.X[c][e]);
-    }
-  }
-}
-
-// Sweep 1 of the block backward in world coordinates (orthonormal base frame): thread total of the
-// local prefix, of g and of Q = sum p (x) g with p the local position.
-template <typename T, int kC, typename V, typename StepFn>
-__device__ __forceinline__ Affine<V> sweep_backward_totals_world(const ChainViews<T, kC>& cv, StepRange r, StepFn step, V (&gsum)[3], V (&Q)[9]) {
-  Affine<V> P = affine_identity<V>();
-#pragma unroll
-  for (int i = 0; i < 3; ++i) gsum[i] = splat<V>(0);
-#pragma unroll
-  for (int i = 0; i < 9; ++i) Q[i] = splat<V>(0);
-  int off = 3 * (r.first + 3);
-#pragma unroll 2
-  for (int k = 0; k < r.count; ++k, off += 3) {
-    advance(P, step(r.first + k));
-    const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
-#pragma unroll
-    for (int c = 0; c < 3; ++c) gsum[c] = vadd(gsum[c], g[c]);
-#pragma unroll
-    for (int d = 0; d < 3; ++d) {
-#pragma unroll
-      for (int c = 0; c < 3; ++c) Q[3 * d + c] = vfma(P.v[d], g[c], Q[3 * d + c]);
-    }
-  }
-  return P;
 }
 
 // Sweep 2 of the block backward: prefix from the carry, gradients from the running suffix.
-// kWorld: carry, positions and gradients in world coordinates (orthonormal base frame).
-// Otherwise base-frame coordinates with g~ = F^T g, plus the per-step first-frame term `acc`
+// kWorld: carry, positions and gradients in world coordinates.  Otherwise base-frame coordinates
+// with g~ = F^T g, plus the per-step first-frame term `acc`
 // (sum_j (g~_j.av) x~_j[0] + (g~_j.bv) x~_j[1]) that a non-orthonormal frame needs.
-template <bool kWorld, typename T, int kC, typename V, typename StepFn>
-__device__ __forceinline__ V block_backward_sweep2(const ChainViews<T, kC>& cv, const V* F, const Affine<V>& carry, V* Fs, V* Ms, const V* av,
-                                                   const V* bv, StepRange r, StepFn step) {
+template <bool kWorld, typename T, typename V, typename StepFn>
+__device__ __forceinline__ V block_backward_sweep2(const ChainViews<T>& cv, const V* F, const Affine<V>& carry, V* Fs, V* Ms, const V* av, const V* bv,
+                                                   StepRange r, StepFn step) {
+  using R = typename ComputeOf<T>::type;
   Affine<V> P = carry;
-  V acc = splat<V>(0);
+  V acc = V(0);
   int off = 3 * (r.first + 3);
 #pragma unroll 2
   for (int k = 0; k < r.count; ++k, off += 3) {
@@ -459,12 +344,12 @@ __device__ __forceinline__ V block_backward_sweep2(const ChainViews<T, kC>& cv, 
     const V xp[3] = {P.v[0], P.v[1], P.v[2]};
     advance(P, step(r.first + k));
     V g[3];
-    if constexpr (kWorld) {
+    if constexpr (kWorld || std::is_same_v<T, R>) {
       g[0] = cv.grad(off);
       g[1] = cv.grad(off + 1);
       g[2] = cv.grad(off + 2);
     } else {
-      base_grad<T, kC, V>(cv, off, F, g);
+      to_base(F, cv.grad(off), cv.grad(off + 1), cv.grad(off + 2), g);
     }
     // tau = Ms - xp x Fs
     V xf[3];
@@ -491,177 +376,300 @@ __device__ __forceinline__ V block_backward_sweep2(const ChainViews<T, kC>& cv, 
   return acc;
 }
 
-// The body of the block backward after staging, for one coordinate choice (see sweep 2).
-template <bool kWorld, typename T, int kC, typename V, typename StepFn>
-__device__ __forceinline__ void block_backward_body(const ChainViews<T, kC>& cv, CtaExchange<V>& ex, const AnchorFrame<typename ComputeOf<T>::type>& af,
-                                                    const ChainFrame<V>& ff, const V* av, const V* bv, V l1, const T* grad_xyz,
-                                                    const int64_t* chain_of, int N, StepRange range, int nwarps, StepFn step) {
-  using R = typename ComputeOf<T>::type;
+// First-frame quantities of the block backward shared by both forms.
+template <typename V>
+struct BackwardFrame {
+  ChainFrame<V> ff;
+  V av[3], bv[3];  // F^T d_dir and F^T (normal x d_dir) (block.cu:224-227)
+  V l1;
+  bool general;    // base frame not orthonormal: use base coordinates
+};
+
+template <typename V, typename S>
+__device__ __forceinline__ BackwardFrame<V> backward_frame(const AnchorFrame<S>& af, V l0, V l1, V a0) {
+  BackwardFrame<V> b;
+  b.ff = chain_frame<V>(af, l0, l1, a0);
+  b.l1 = l1;
+  V d_dir[3], d_side[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) d_dir[i] = vfma(b.ff.c0, V(af.turn0[i]), vmul(b.ff.s0, V(af.dir0[i])));
+  cross3(b.ff.normal, d_dir, d_side);
+  to_base(b.ff.F, d_dir[0], d_dir[1], d_dir[2], b.av);
+  to_base(b.ff.F, d_side[0], d_side[1], d_side[2], b.bv);
+  // For an orthonormal right-handed F, av = -sigma e_y and bv = sigma e_x (sigma = sign sin a0).
+  const V dev = fabs(b.av[0]) + fabs(b.av[2]) + fabs(b.bv[1]) + fabs(b.bv[2]) + fabs(b.av[1] + b.bv[0]);
+  b.general = !(dev <= static_cast<V>(1e-5) && fabs(b.bv[0]) >= static_cast<V>(0.5));
+  return b;
+}
+
+// Gradients of lengths[0], lengths[1] and angles[0] (write_first_frame_param_grads,
+// block.cu:206-228) into atom slots 1 and 2, by thread 0.  F3 and M3 are the suffix sums over every
+// atom >= 3 (world coordinates) or F3 in base coordinates and `acc` the reduced first-frame term
+// (base coordinates).
+template <bool kWorld, typename T, typename V>
+__device__ __forceinline__ void first_frame_grads(const ChainViews<T>& cv, const AnchorFrame<V>& af, const BackwardFrame<V>& bf, const T* grow, const V* F3,
+                                                  const V* M3, V acc) {
+  const ChainFrame<V>& ff = bf.ff;
+  V g1[3], g2[3], grad_p2[3], d_dir[3], dir0[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    g1[i] = to_r<V>(grow[3 + i]);
+    g2[i] = to_r<V>(grow[6 + i]);
+    dir0[i] = af.dir0[i];
+    d_dir[i] = vfma(ff.c0, V(af.turn0[i]), vmul(ff.s0, dir0[i]));
+  }
+  if constexpr (kWorld) {
+    // the z moment about p2 in base coordinates is normal . (M3 - p2 x F3); for an orthonormal frame
+    // the first-frame projection term is -bv[0] times it
+    V pf[3];
+    cross3(ff.p2, F3, pf);
+    const V m_about_p2[3] = {vsub(M3[0], pf[0]), vsub(M3[1], pf[1]), vsub(M3[2], pf[2])};
+    acc = vneg(vmul(bf.bv[0], dot3(ff.normal, m_about_p2)));
+#pragma unroll
+    for (int i = 0; i < 3; ++i) grad_p2[i] = vadd(g2[i], F3[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) grad_p2[i] = vfma(ff.F[3 * i + 2], F3[2], vfma(ff.F[3 * i + 1], F3[1], vfma(ff.F[3 * i + 0], F3[0], g2[i])));
+  }
+  V g12[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) g12[i] = vadd(g1[i], grad_p2[i]);
+  cv.set_slot(3, dot3(g12, dir0));
+  cv.set_slot(6, dot3(grad_p2, ff.dir1));
+  cv.set_slot(7, vfma(bf.l1, dot3(grad_p2, d_dir), acc));
+}
+
+// Recompute backward after staging, for one coordinate choice.
+template <bool kWorld, typename T, typename V, typename StepFn>
+__device__ __forceinline__ void block_backward_recompute(const ChainViews<T>& cv, CtaExchange<V>& ex, const AnchorFrame<V>& af, const BackwardFrame<V>& bf,
+                                                      const T* grow, StepRange range, int nwarps, StepFn step) {
   V gsum[3];
   V Q[9];
-  Affine<V> carry;
-  if constexpr (kWorld) {
-    const Affine<V> total = sweep_backward_totals_world<T, kC, V>(cv, range, step, gsum, Q);
-    Affine<V> base;  // the base frame (F, p2): world = base * chain-local prefix
-#pragma unroll
-    for (int i = 0; i < 9; ++i) base.m[i] = ff.F[i];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) base.v[i] = ff.p2[i];
-    carry = compose(base, cta_exclusive_affine<V>(total, ex.warp_totals, nwarps));
-  } else {
-    const Affine<V> total = sweep_backward_totals<T, kC, V>(cv, ff.F, range, step, gsum, Q);
-    carry = cta_exclusive_affine<V>(total, ex.warp_totals, nwarps);
-  }
+  const Affine<V> total = sweep_backward_totals<kWorld, T, V>(cv, bf.ff.F, range, step, gsum, Q);
+  Affine<V> carry = cta_exclusive_affine<V>(total, ex.warp_totals, nwarps);
+  if constexpr (kWorld) carry = world_carry(carry, bf.ff.F, bf.ff.p2);
+  V msum[3];
+  moment_total<V>(carry, gsum, Q, msum);
   V Fs[3], Ms[3];
-  suffix_base<V>(carry, gsum, Q, ex, nwarps, Fs, Ms);
-  // thread 0's suffix base covers every atom >= 3 (S_0 of the reference)
+  suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
   const V F3[3] = {Fs[0], Fs[1], Fs[2]};
   const V M3[3] = {Ms[0], Ms[1], Ms[2]};
-  V acc = block_backward_sweep2<kWorld, T, kC, V>(cv, ff.F, carry, Fs, Ms, av, bv, range, step);
+  V acc = block_backward_sweep2<kWorld, T, V>(cv, bf.ff.F, carry, Fs, Ms, bf.av, bf.bv, range, step);
   if constexpr (!kWorld) acc = cta_sum_to_thread0<V>(acc, ex.warp_red, nwarps);
-  if (threadIdx.x == 0) {
-    V g1[3], g2[3], grad_p2[3], d_dir[3], dir0[3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      if constexpr (kC == 2) {
-        g1[i] = make_float2(to_r<float>(grad_xyz[chain_of[0] * 3 * N + 3 + i]), to_r<float>(grad_xyz[chain_of[1] * 3 * N + 3 + i]));
-        g2[i] = make_float2(to_r<float>(grad_xyz[chain_of[0] * 3 * N + 6 + i]), to_r<float>(grad_xyz[chain_of[1] * 3 * N + 6 + i]));
-      } else {
-        g1[i] = to_r<R>(grad_xyz[chain_of[0] * 3 * N + 3 + i]);
-        g2[i] = to_r<R>(grad_xyz[chain_of[0] * 3 * N + 6 + i]);
-      }
-      dir0[i] = splat<V>(af.dir0[i]);
-      d_dir[i] = vfma(ff.c0, splat<V>(af.turn0[i]), vmul(ff.s0, dir0[i]));
-    }
-    if constexpr (kWorld) {
-      // sum_{j>=3} g_j is F3 in world coordinates; the z moment about p2 in base coordinates is
-      // normal . (M3 - p2 x F3), and for an orthonormal frame the projection term is -bv[0] times it
-      V pf[3];
-      cross3(ff.p2, F3, pf);
-      const V m_about_p2[3] = {vsub(M3[0], pf[0]), vsub(M3[1], pf[1]), vsub(M3[2], pf[2])};
-      acc = vneg(vmul(bv[0], dot3(ff.normal, m_about_p2)));
-#pragma unroll
-      for (int i = 0; i < 3; ++i) grad_p2[i] = vadd(g2[i], F3[i]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 3; ++i) grad_p2[i] = vfma(ff.F[3 * i + 2], F3[2], vfma(ff.F[3 * i + 1], F3[1], vfma(ff.F[3 * i + 0], F3[0], g2[i])));
-    }
-    V g12[3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) g12[i] = vadd(g1[i], grad_p2[i]);
-    cv.set_slot(3, dot3(g12, dir0));
-    cv.set_slot(6, dot3(grad_p2, ff.dir1));
-    cv.set_slot(7, vfma(l1, dot3(grad_p2, d_dir), acc));
+  if (threadIdx.x == 0) first_frame_grads<kWorld, T, V>(cv, af, bf, grow, F3, M3, acc);
+}
+
+// The base-coordinate form, for a base frame that is not orthonormal.
+template <typename T, typename V, typename StepFn>
+__device__ __forceinline__ void block_backward_general(const ChainViews<T>& cv, CtaExchange<V>& ex, const AnchorFrame<V>& af, const BackwardFrame<V>& bf,
+                                                    const T* grow, StepRange range, int nwarps, StepFn step) {
+  block_backward_recompute<false, T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+}
+
+template <typename T>
+__device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* grad_lengths, T* grad_angles, T* grad_dihedrals, int64_t chain, int N, int tid,
+                                                  int nthr) {
+  using R = typename ComputeOf<T>::type;
+  T* gl = grad_lengths + chain * (N - 1);
+  T* ga = grad_angles + chain * (N - 2);
+  T* gd = grad_dihedrals + chain * (N - 3);
+  const R* X = cv.X;
+#pragma unroll 2
+  for (int i = tid; i < N - 1; i += nthr) {
+    const R* slot = X + 3 * i;
+    gl[i] = from_r<T>(slot[3]);
+    if (i < N - 2) ga[i] = from_r<T>(slot[7]);
+    if (i < N - 3) gd[i] = from_r<T>(slot[11]);
   }
 }
 
-template <typename T, int kC>
-__global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockArgs<T> args, const T* __restrict__ grad_xyz,
-                                                                         T* __restrict__ grad_lengths, T* __restrict__ grad_angles,
-                                                                         T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+// --------------------------------------------------------------------------------------------
+// block path
+// --------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, typename ComputeOf<T>::type* __restrict__ state, ChainGeometry geo) {
   using R = typename ComputeOf<T>::type;
-  using S = R;
-  using V = LaneOf<R, kC>;
+  using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
   const int N = geo.points, St = geo.steps, K = geo.items;
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const size_t region = block_region_bytes<T>(N, true);
-  ChainViews<T, kC> cv;
-  int64_t chain_of[kC];
-  bool valid[kC];
-#pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const int64_t chain = cta_chain<kC>(c, geo.batch, valid[c]);
-    chain_of[c] = chain;
-    const T* Lr = args.lengths + chain * (N - 1);
-    const T* Ar = args.angles + chain * (N - 2);
-    const T* Dr = args.dihedrals + chain * (N - 3);
-    unsigned char* p = smem + c * region;
-    cv.X[c] = reinterpret_cast<R*>(p);
-    p += slot_bytes(N, sizeof(R));
-    if constexpr (kScatter) {
-      scatter_block_inputs<T>(reinterpret_cast<T*>(cv.X[c]), Lr, Ar, Dr, N, tid, nthr);
-    } else {
-      cv.row[c][0] = stage_row_async(p, Lr, N - 1, tid, nthr);
-      p += staged_row_bytes(N - 1, sizeof(T));
-      cv.row[c][1] = stage_row_async(p, Ar, N - 2, tid, nthr);
-      p += staged_row_bytes(N - 2, sizeof(T));
-      cv.row[c][2] = stage_row_async(p, Dr, N - 3, tid, nthr);
-      p += staged_row_bytes(N - 3, sizeof(T));
-    }
-    cv.G[c] = stage_row_async(p, grad_xyz + chain * 3 * N, 3 * N, tid, nthr);
-  }
-  const AnchorFrame<S> af = anchor_frame<S>(args.p0, args.first_direction, args.initial_normal);
+  const int64_t chain = blockIdx.x;
+  T* out = xyz + chain * 3 * N;
+  ChainViews<T> cv;
+  stage_block_inputs<T>(cv, smem, args, chain, N, kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : 0, tid, nthr);
+  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
   cp_async_wait_all();
   __syncthreads();
 
-  V l0, l1, a0;
-  if constexpr (kScatter) {
-    l0 = cv.slot(3);
-    l1 = cv.slot(6);
-    a0 = cv.slot(7);
-  } else {
-    l0 = cv.staged(0, 0);
-    l1 = cv.staged(0, 1);
-    a0 = cv.staged(1, 0);
-  }
-  const ChainFrame<V> ff = chain_frame<V>(af, l0, l1, a0);
-  // projections of write_first_frame_param_grads (block.cu:224-227) in base coordinates
-  V av[3], bv[3];
+  V F[9], p2[3];
   {
-    V d_dir[3], d_side[3];
+    V l0, l1, a0;
+    first_inputs(cv, l0, l1, a0);
+    const ChainFrame<V> ff = chain_frame<V>(af, l0, l1, a0);
 #pragma unroll
-    for (int i = 0; i < 3; ++i) d_dir[i] = vfma(ff.c0, splat<V>(af.turn0[i]), vmul(ff.s0, splat<V>(af.dir0[i])));
-    cross3(ff.normal, d_dir, d_side);
-    to_base(ff.F, d_dir[0], d_dir[1], d_dir[2], av);
-    to_base(ff.F, d_side[0], d_side[1], d_side[2], bv);
-  }
-  // For an orthonormal right-handed F, av = -sigma e_y and bv = sigma e_x (sigma = sign sin a0): the
-  // whole backward can then run in world coordinates.  Otherwise (degenerate anchors or a collinear
-  // first angle) it runs in base coordinates with the reference's general first-frame term.
-  bool general = false;
+    for (int i = 0; i < 9; ++i) F[i] = ff.F[i];
 #pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const S tol = static_cast<S>(1e-5);
-    const S a0_ = lane(av[0], c), a1_ = lane(av[1], c), a2_ = lane(av[2], c);
-    const S b0_ = lane(bv[0], c), b1_ = lane(bv[1], c), b2_ = lane(bv[2], c);
-    const S dev = fabs(a0_) + fabs(a2_) + fabs(b1_) + fabs(b2_) + fabs(a1_ + b0_);
-    general = general || !(dev <= tol && fabs(b0_) >= static_cast<S>(0.5));
+    for (int i = 0; i < 3; ++i) p2[i] = ff.p2[i];
+    if constexpr (kScatter) __syncthreads();  // every thread has read l0, l1, a0 from atom slots 1, 2
+    if (tid == 0) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        cv.set_slot(i, af.p0[i]);
+        cv.set_slot(3 + i, ff.p1[i]);
+        cv.set_slot(6 + i, ff.p2[i]);
+      }
+    }
   }
 
   auto step = [&](int s) {
     V l, th, ph, st, ct, sp, cp;
-    block_step_inputs<T, kC>(cv, s, l, th, ph);
+    block_step_inputs<T>(cv, s, l, th, ph);
     step_sincos(th, ph, st, ct, sp, cp);
     return step_rot(l, st, ct, sp, cp);
   };
 
   const StepRange range = step_range(tid, K, St);
-  if (general) {
-    block_backward_body<false, T, kC, V>(cv, ex, af, ff, av, bv, l1, grad_xyz, chain_of, N, range, nwarps, step);
+  const Affine<V> total = sweep_local_prefix<T, V>(cv, range, step);
+  const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
+  apply_carry<T, V>(cv, W, range);
+  if (state != nullptr) {
+    R* dst = state + (chain * nthr + tid) * kStateWords;
+#pragma unroll
+    for (int i = 0; i < 9; ++i) dst[i] = W.m[i];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) dst[9 + i] = W.v[i];
+  }
+  store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockArgs<T> args, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
+                                                                         T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const int64_t chain = blockIdx.x;
+  const T* grow = grad_xyz + chain * 3 * N;
+  ChainViews<T> cv;
+  unsigned char* p = stage_block_inputs<T>(cv, smem, args, chain, N, 0, tid, nthr);
+  cv.G = stage_row_async(p, grow, 3 * N, tid, nthr);
+  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+  cp_async_wait_all();
+  __syncthreads();
+
+  V l0, l1, a0;
+  first_inputs(cv, l0, l1, a0);
+  const BackwardFrame<V> bf = backward_frame<V>(af, l0, l1, a0);
+  auto step = [&](int s) {
+    V l, th, ph, st, ct, sp, cp;
+    block_step_inputs<T>(cv, s, l, th, ph);
+    step_sincos(th, ph, st, ct, sp, cp);
+    return step_rot(l, st, ct, sp, cp);
+  };
+  const StepRange range = step_range(tid, K, St);
+  if (bf.general) {
+    block_backward_general<T, V>(cv, ex, af, bf, grow, range, nwarps, step);
   } else {
-    block_backward_body<true, T, kC, V>(cv, ex, af, ff, av, bv, l1, grad_xyz, chain_of, N, range, nwarps, step);
+    block_backward_recompute<true, T, V>(cv, ex, af, bf, grow, range, nwarps, step);
   }
   __syncthreads();
+  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);
+}
+
+// Backward from the forward's xyz and saved state (4- and 8-byte types; the launch plan must be the
+// forward's).  Shared memory holds two rows: the staged gradient row G and a slot row that first
+// receives the forward's xyz (for the thread sums of g and x x g) and then the scattered inputs (for
+// sweep 2), whose loads overlap the suffix scan.  A chain whose base frame is not orthonormal
+// falls back to the recompute form.
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    block_backward_saved_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const typename ComputeOf<T>::type* __restrict__ state,
+                                const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths, T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals,
+                                ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  static_assert(sizeof(T) >= 4, "the saved form serves 32- and 64-bit types");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const int64_t chain = blockIdx.x;
+  const T* grow = grad_xyz + chain * 3 * N;
+  ChainViews<T> cv;
+  unsigned char* slot_region = smem;
+  cv.X = reinterpret_cast<R*>(slot_region);
+  cv.G = stage_row_async(smem + slot_bytes(N, sizeof(R)), grow, 3 * N, tid, nthr);
+  cv.Y = stage_row_async(slot_region, xyz + chain * 3 * N, 3 * N, tid, nthr);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+  const R l0 = args.lengths[chain * (N - 1)];
+  const R l1 = args.lengths[chain * (N - 1) + 1];
+  const R a0 = args.angles[chain * (N - 2)];
+  const BackwardFrame<V> bf = backward_frame<V>(af, l0, l1, a0);
+  auto step = [&](int s) {
+    V l, th, ph, st, ct, sp, cp;
+    block_step_inputs<T>(cv, s, l, th, ph);
+    step_sincos(th, ph, st, ct, sp, cp);
+    return step_rot(l, st, ct, sp, cp);
+  };
+  const StepRange range = step_range(tid, K, St);
+  if (bf.general) {
+    // recompute form: inputs into the slots, gradients staged as for block_backward_kernel
+    cp_async_wait_all();
+    __syncthreads();
+    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
+    cp_async_wait_all();
+    __syncthreads();
+    block_backward_general<T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+  } else {
+    Affine<V> carry;
+    {
+      const R* src = state + (chain * nthr + tid) * kStateWords;
 #pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    if (!valid[c]) continue;
-    const int64_t chain = chain_of[c];
-    T* gl = grad_lengths + chain * (N - 1);
-    T* ga = grad_angles + chain * (N - 2);
-    T* gd = grad_dihedrals + chain * (N - 3);
-    const R* X = cv.X[c];
-#pragma unroll 2
-    for (int i = tid; i < N - 1; i += nthr) {
-      const R* slot = X + 3 * i;
-      gl[i] = from_r<T>(slot[3]);
-      if (i < N - 2) ga[i] = from_r<T>(slot[7]);
-      if (i < N - 3) gd[i] = from_r<T>(slot[11]);
+      for (int i = 0; i < 9; ++i) carry.m[i] = src[i];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) carry.v[i] = src[9 + i];
     }
+    cp_async_wait_all();
+    __syncthreads();
+    // thread sums of g and x x g straight from the staged rows
+    V gsum[3] = {V(0), V(0), V(0)};
+    V msum[3] = {V(0), V(0), V(0)};
+    int off = 3 * (range.first + 3);
+#pragma unroll 4
+    for (int k = 0; k < range.count; ++k, off += 3) {
+      const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+      const V x[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+      V mx[3];
+      cross3(x, g, mx);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        gsum[i] = vadd(gsum[i], g[i]);
+        msum[i] = vadd(msum[i], mx[i]);
+      }
+    }
+    __syncthreads();  // the xyz row is consumed: the slot row now takes the inputs
+    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
+    V Fs[3], Ms[3];
+    suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
+    const V F3[3] = {Fs[0], Fs[1], Fs[2]};
+    const V M3[3] = {Ms[0], Ms[1], Ms[2]};
+    cp_async_wait_all();
+    __syncthreads();
+    block_backward_sweep2<true, T, V>(cv, bf.ff.F, carry, Fs, Ms, bf.av, bf.bv, range, step);
+    if (tid == 0) first_frame_grads<true, T, V>(cv, af, bf, grow, F3, M3, V(0));
   }
+  __syncthreads();
+  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);
 }
 
 // --------------------------------------------------------------------------------------------
@@ -669,42 +677,31 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
 // --------------------------------------------------------------------------------------------
 
 // Fixed base frame of the torsion path (make_default_base_frame, torsion.cu:149-166).
-template <typename V, typename R>
-__device__ __forceinline__ void torsion_base(const TorsionConsts<R>& c, V* F, V* p1, V* p2) {
-  const R s = c.sin_a[0], co = c.cos_a[0];
+template <typename V>
+__device__ __forceinline__ void torsion_base(const TorsionConsts<V>& c, V* F, V* p1, V* p2) {
+  const V s = c.sin_a[0], co = c.cos_a[0];
   // columns dir1 = (-c, s, 0), side = (-s, -c, 0), normal = (0, 0, 1)
-  const R f[9] = {-co, -s, R(0), s, -co, R(0), R(0), R(0), R(1)};
+  const V f[9] = {-co, -s, V(0), s, -co, V(0), V(0), V(0), V(1)};
 #pragma unroll
-  for (int i = 0; i < 9; ++i) F[i] = splat<V>(f[i]);
-  p1[0] = splat<V>(c.length[0]);
-  p1[1] = splat<V>(R(0));
-  p1[2] = splat<V>(R(0));
-  p2[0] = splat<V>(c.length[0] - c.length[1] * co);
-  p2[1] = splat<V>(c.length[1] * s);
-  p2[2] = splat<V>(R(0));
+  for (int i = 0; i < 9; ++i) F[i] = f[i];
+  p1[0] = c.length[0];
+  p1[1] = V(0);
+  p1[2] = V(0);
+  p2[0] = c.length[0] - c.length[1] * co;
+  p2[1] = c.length[1] * s;
+  p2[2] = V(0);
 }
 
 // |(s, c)|^2 clamped below at 1e-8f * 1e-8f (clamped_pair_norm2, torsion.cu:119-123)
 template <typename V>
 __device__ __forceinline__ V torsion_norm2(V s, V c) {
   const V n2 = vfma(s, s, vmul(c, c));
-  return lanewise(n2, [](auto x) {
-    using S = decltype(x);
-    const S eps2 = static_cast<S>(1.0e-8f * 1.0e-8f);
-    return x < eps2 ? eps2 : x;
-  });
+  const V eps2 = static_cast<V>(1.0e-8f * 1.0e-8f);
+  return n2 < eps2 ? eps2 : n2;
 }
 // 1/sqrt(n2): rsqrtf in float (the reference builds this path with fast math), 1/sqrt in double
-template <typename V>
-__device__ __forceinline__ V torsion_rinv(V n2) {
-  return lanewise(n2, [](auto x) {
-    if constexpr (std::is_same_v<decltype(x), float>) {
-      return rsqrtf(x);
-    } else {
-      return 1.0 / sqrt(x);
-    }
-  });
-}
+__device__ __forceinline__ float torsion_rinv(float n2) { return rsqrtf(n2); }
+__device__ __forceinline__ double torsion_rinv(double n2) { return 1.0 / sqrt(n2); }
 
 // step s uses length phase (s+2)%3 and angle phase (s+1)%3 (torsion.cu:67-73, 219-236)
 template <typename R>
@@ -721,9 +718,8 @@ __device__ __forceinline__ void scatter_pairs(T* X, const T* raw, int S, int tid
   for (int e = tid; e < 2 * S; e += nthr) cp_async<sizeof(T)>(X + 3 * ((e >> 1) + 3) + 1 + (e & 1), raw + e);
 }
 
-template <typename T, int kC>
-__device__ __forceinline__ void torsion_pair(const ChainViews<T, kC>& cv, int s, LaneOf<typename ComputeOf<T>::type, kC>& rs,
-                                             LaneOf<typename ComputeOf<T>::type, kC>& rc) {
+template <typename T>
+__device__ __forceinline__ void torsion_pair(const ChainViews<T>& cv, int s, typename ComputeOf<T>::type& rs, typename ComputeOf<T>::type& rc) {
   if constexpr (sizeof(T) >= 4) {
     rs = cv.slot(3 * (s + 3) + 1);
     rc = cv.slot(3 * (s + 3) + 2);
@@ -733,42 +729,35 @@ __device__ __forceinline__ void torsion_pair(const ChainViews<T, kC>& cv, int s,
   }
 }
 
-template <typename T, int kC>
+template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
-    torsion_forward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
-                           T* __restrict__ xyz, ChainGeometry geo) {
+    torsion_forward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts, T* __restrict__ xyz,
+                           ChainGeometry geo) {
   using R = typename ComputeOf<T>::type;
-  using V = LaneOf<R, kC>;
+  using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
   const int N = geo.points, St = geo.steps, K = geo.items;
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const size_t region = torsion_region_bytes<T>(N, false);
-  ChainViews<T, kC> cv;
-  T* out[kC];
-  bool valid[kC];
-  V F[9], p1[3], p2[3];
-  torsion_base<V, R>(consts, F, p1, p2);
-#pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const int64_t chain = cta_chain<kC>(c, geo.batch, valid[c]);
-    const T* raw = raw_pairs + chain * raw_stride;
-    out[c] = xyz + chain * 3 * N;
-    unsigned char* base = smem + c * region;
-    if constexpr (kScatter) {
-      cv.X[c] = reinterpret_cast<R*>(base + (reinterpret_cast<uintptr_t>(out[c]) & 15u));
-      scatter_pairs<T>(reinterpret_cast<T*>(cv.X[c]), raw, St, tid, nthr);
-    } else {
-      cv.X[c] = reinterpret_cast<R*>(base);
-      cv.row[c][0] = stage_row_async(base + slot_bytes(N, sizeof(R)), raw, 2 * St, tid, nthr);
-    }
+  const int64_t chain = blockIdx.x;
+  const T* raw = raw_pairs + chain * raw_stride;
+  T* out = xyz + chain * 3 * N;
+  ChainViews<T> cv;
+  if constexpr (kScatter) {
+    cv.X = reinterpret_cast<R*>(smem + (reinterpret_cast<uintptr_t>(out) & 15u));
+    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
+  } else {
+    cv.X = reinterpret_cast<R*>(smem);
+    cv.row[0] = stage_row_async(smem + slot_bytes(N, sizeof(R)), raw, 2 * St, tid, nthr);
   }
+  V F[9], p1[3], p2[3];
+  torsion_base<V>(consts, F, p1, p2);
   if (tid == 0) {  // atom slots 0..2 receive no input
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      cv.set_slot(i, splat<V>(R(0)));
+      cv.set_slot(i, V(0));
       cv.set_slot(3 + i, p1[i]);
       cv.set_slot(6 + i, p2[i]);
     }
@@ -778,90 +767,69 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
 
   auto step = [&](int s) {
     V rs, rc;
-    torsion_pair<T, kC>(cv, s, rs, rc);
+    torsion_pair<T>(cv, s, rs, rc);
     const V rinv = torsion_rinv(torsion_norm2(rs, rc));
     R l, st, ct;
     torsion_constants_for(consts, s, l, st, ct);
-    return step_rot(splat<V>(l), splat<V>(st), splat<V>(ct), vmul(rs, rinv), vmul(rc, rinv));
+    return step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv));
   };
 
   const StepRange range = step_range(tid, K, St);
-  const Affine<V> total = sweep_local_prefix<T, kC, V>(cv, range, step);
-  const Affine<V> carry = cta_exclusive_affine<V>(total, ex.warp_totals, nwarps);
-  apply_carry<T, kC, V>(cv, carry, F, p2, range);
-
-  if constexpr (kScatter) {
-    fence_proxy_async_smem();
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      if (valid[c]) store_row_bulk<T>(out[c], reinterpret_cast<const T*>(cv.X[c]), 3 * N, tid, nthr, c);
-    }
-    if (tid < kC) bulk_store_wait_read();
-  } else {
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      if (!valid[c]) continue;
-#pragma unroll 4
-      for (int e = tid; e < 3 * N; e += nthr) out[c][e] = from_r<T>(cv.X[c][e]);
-    }
-  }
+  const Affine<V> total = sweep_local_prefix<T, V>(cv, range, step);
+  const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
+  apply_carry<T, V>(cv, W, range);
+  store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 
-template <typename T, int kC>
+template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_backward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
                             const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride, ChainGeometry geo) {
   using R = typename ComputeOf<T>::type;
-  using V = LaneOf<R, kC>;
+  using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
   const int N = geo.points, St = geo.steps, K = geo.items;
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const size_t region = torsion_region_bytes<T>(N, true);
-  ChainViews<T, kC> cv;
-  int64_t chain_of[kC];
-  bool valid[kC];
-#pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const int64_t chain = cta_chain<kC>(c, geo.batch, valid[c]);
-    chain_of[c] = chain;
-    const T* raw = raw_pairs + chain * raw_stride;
-    unsigned char* p = smem + c * region;
-    cv.X[c] = reinterpret_cast<R*>(p);
-    p += slot_bytes(N, sizeof(R));
-    if constexpr (kScatter) {
-      scatter_pairs<T>(reinterpret_cast<T*>(cv.X[c]), raw, St, tid, nthr);
-    } else {
-      cv.row[c][0] = stage_row_async(p, raw, 2 * St, tid, nthr);
-      p += staged_row_bytes(size_t(2) * St, sizeof(T));
-    }
-    cv.G[c] = stage_row_async(p, grad_xyz + chain * 3 * N, 3 * N, tid, nthr);
+  const int64_t chain = blockIdx.x;
+  const T* raw = raw_pairs + chain * raw_stride;
+  ChainViews<T> cv;
+  unsigned char* p = smem;
+  cv.X = reinterpret_cast<R*>(p);
+  p += slot_bytes(N, sizeof(R));
+  if constexpr (kScatter) {
+    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
+  } else {
+    cv.row[0] = stage_row_async(p, raw, 2 * St, tid, nthr);
+    p += staged_row_bytes(size_t(2) * St, sizeof(T));
   }
+  cv.G = stage_row_async(p, grad_xyz + chain * 3 * N, 3 * N, tid, nthr);
   V F[9], p1[3], p2[3];
-  torsion_base<V, R>(consts, F, p1, p2);
+  torsion_base<V>(consts, F, p1, p2);
   cp_async_wait_all();
   __syncthreads();
 
   auto step = [&](int s) {
     V rs, rc;
-    torsion_pair<T, kC>(cv, s, rs, rc);
+    torsion_pair<T>(cv, s, rs, rc);
     const V rinv = torsion_rinv(torsion_norm2(rs, rc));
     R l, st, ct;
     torsion_constants_for(consts, s, l, st, ct);
-    return step_rot(splat<V>(l), splat<V>(st), splat<V>(ct), vmul(rs, rinv), vmul(rc, rinv));
+    return step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv));
   };
 
+  // the fixed torsion base frame is orthonormal: world coordinates throughout
   const StepRange range = step_range(tid, K, St);
   V gsum[3];
   V Q[9];
-  const Affine<V> total = sweep_backward_totals<T, kC, V>(cv, F, range, step, gsum, Q);
-  const Affine<V> carry = cta_exclusive_affine<V>(total, ex.warp_totals, nwarps);
+  const Affine<V> total = sweep_backward_totals<true, T, V>(cv, F, range, step, gsum, Q);
+  const Affine<V> carry = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
+  V msum[3];
+  moment_total<V>(carry, gsum, Q, msum);
   V Fs[3], Ms[3];
-  suffix_base<V>(carry, gsum, Q, ex, nwarps, Fs, Ms);
+  suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
 
   Affine<V> P = carry;
   int off = 3 * (range.first + 3);
@@ -869,43 +837,36 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   for (int k = 0; k < range.count; ++k, off += 3) {
     const int s = range.first + k;
     const V u0 = P.m[0], u1 = P.m[3], u2 = P.m[6];
-    const V nxp[3] = {vneg(P.v[0]), vneg(P.v[1]), vneg(P.v[2])};
+    const V xp[3] = {P.v[0], P.v[1], P.v[2]};
     V rs, rc;
-    torsion_pair<T, kC>(cv, s, rs, rc);
+    torsion_pair<T>(cv, s, rs, rc);
     const V n2 = torsion_norm2(rs, rc);
     const V rinv = torsion_rinv(n2);
     R l, st, ct;
     torsion_constants_for(consts, s, l, st, ct);
-    advance(P, step_rot(splat<V>(l), splat<V>(st), splat<V>(ct), vmul(rs, rinv), vmul(rc, rinv)));
-    V gt[3];
-    base_grad<T, kC, V>(cv, off, F, gt);
-    V tau[3];
-    tau[0] = vfma(nxp[1], Fs[2], vfma(vneg(nxp[2]), Fs[1], Ms[0]));
-    tau[1] = vfma(nxp[2], Fs[0], vfma(vneg(nxp[0]), Fs[2], Ms[1]));
-    tau[2] = vfma(nxp[0], Fs[1], vfma(vneg(nxp[1]), Fs[0], Ms[2]));
+    advance(P, step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv)));
+    const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+    V xf[3];
+    cross3(xp, Fs, xf);
+    const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
     const V d_phi = vfma(u2, tau[2], vfma(u1, tau[1], vmul(u0, tau[0])));
     V mx[3];
-    cross3(P.v, gt, mx);
+    cross3(P.v, g, mx);
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      Fs[i] = vsub(Fs[i], gt[i]);
+      Fs[i] = vsub(Fs[i], g[i]);
       Ms[i] = vsub(Ms[i], mx[i]);
     }
     // raw-pair chain rule (torsion.cu:173-182): d raw = d phi * (c, -s) / n2
-    const V scale = lanewise(n2, [](auto x) { return decltype(x)(1) / x; });
-    const V g = vmul(d_phi, scale);
-    cv.set_slot(off + 1, vmul(rc, g));
-    cv.set_slot(off + 2, vneg(vmul(rs, g)));
+    const V scale = d_phi / n2;
+    cv.set_slot(off + 1, vmul(rc, scale));
+    cv.set_slot(off + 2, vneg(vmul(rs, scale)));
   }
   __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    if (!valid[c]) continue;
-    T* gr = grad_raw + chain_of[c] * grad_stride;
-    const R* X = cv.X[c];
+  T* gr = grad_raw + chain * grad_stride;
+  const R* X = cv.X;
 #pragma unroll 4
-    for (int e = tid; e < 2 * St; e += nthr) gr[e] = from_r<T>(X[3 * ((e >> 1) + 3) + 1 + (e & 1)]);
-  }
+  for (int e = tid; e < 2 * St; e += nthr) gr[e] = from_r<T>(X[3 * ((e >> 1) + 3) + 1 + (e & 1)]);
 }
 
 }  // namespace cufkb

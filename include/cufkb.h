@@ -26,7 +26,14 @@
 #ifndef CUFKB_H_
 #define CUFKB_H_
 
+#include <stddef.h>
 #include <stdint.h>
+
+#if defined(__GNUC__)
+#define CUFKB_API __attribute__((visibility("default")))
+#else
+#define CUFKB_API
+#endif
 
 #ifdef __cplusplus
 extern "C" {
@@ -70,35 +77,54 @@ typedef struct cufkb_torsion_constants {
 } cufkb_torsion_constants;
 
 /* 2051 = BLOCK_SCAN_MAX_POINT_COUNT (src/cufk/reconstruct.py:5). */
-int cufkb_max_point_count(void);
+CUFKB_API int cufkb_max_point_count(void);
 
 /* xyz (B, N, 3) from lengths/angles/dihedrals and the three optional anchors. */
-int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+CUFKB_API int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                         const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
                         cufkb_stream_t stream);
 
+/* Bytes of the state cufkb_block_forward_save writes for these sizes on the current device (0 for
+ * float16/bfloat16, whose backward always recomputes).  Needs the CUDA device. */
+CUFKB_API int cufkb_block_state_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes);
+
+/* cufkb_block_forward that also writes the per-segment world frames a later
+ * cufkb_block_backward_saved needs (state: cufkb_block_state_bytes bytes, 16-byte aligned, device
+ * memory).  No counterpart in the reference, whose backward always recomputes the chain. */
+CUFKB_API int cufkb_block_forward_save(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                             const void* first_direction, const void* initial_normal, void* xyz, void* state, int64_t batch,
+                             int64_t points, cufkb_stream_t stream);
+
 /* Gradients of sum(grad_xyz * xyz) w.r.t. lengths, angles and dihedrals (no anchor gradients).
  * Recomputes the forward prefix; needs nothing saved from cufkb_block_forward. */
-int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+CUFKB_API int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                          const void* first_direction, const void* initial_normal, const void* grad_xyz, void* grad_lengths,
                          void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream);
 
+/* The same gradients as cufkb_block_backward from the xyz and state of a cufkb_block_forward_save
+ * call with identical arguments on the same device: the chain is walked once instead of twice.
+ * float16/bfloat16 ignore xyz and state and recompute.  Replaces backward_cuda_impl<T> as well. */
+CUFKB_API int cufkb_block_backward_saved(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                               const void* first_direction, const void* initial_normal, const void* xyz, const void* state,
+                               const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                               int64_t points, cufkb_stream_t stream);
+
 /* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
  * elements (any stride >= 0, pairs within a row contiguous). */
-int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+CUFKB_API int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
                           void* xyz, int64_t batch, int64_t points, cufkb_stream_t stream);
 
 /* Gradient w.r.t. the raw pairs; grad row b starts at grad_raw_pairs + b * grad_row_stride
  * (stride >= 2(N-3) when B > 1).  Recomputes the forward; reads no saved xyz. */
-int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+CUFKB_API int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
                            const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
                            cufkb_stream_t stream);
 
 /* Static text for a status code. */
-const char* cufkb_status_string(int status);
+CUFKB_API const char* cufkb_status_string(int status);
 
 /* cudaError_t value of the last CUFKB_ERROR_CUDA returned on the calling thread (0 if none). */
-int cufkb_last_cuda_error(void);
+CUFKB_API int cufkb_last_cuda_error(void);
 
 #ifdef __cplusplus
 }

@@ -24,7 +24,7 @@ class TorsionConstants(ctypes.Structure):
 
 def declared_functions():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(cufkb_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:CUFKB_API\s+)?(?:const\s+)?\w+\*?\s+\*?(cufkb_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -87,6 +87,23 @@ def test_block_backward_validation(lib):
     assert bwd(g=None) == NULL_POINTER
     assert bwd(gd=None) == NULL_POINTER
     assert bwd(gl=82) == MISALIGNED
+
+
+def test_saved_path_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_save.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_backward_saved.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_state_bytes.argtypes = [ctypes.c_int, i64, i64, ctypes.POINTER(ctypes.c_size_t)]
+    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, None, 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, 72, 2, 10, None) == MISALIGNED
+    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, 80, 2, 3, None) == POINT_COUNT
+    assert lib.cufkb_block_backward_saved(F32, 16, 32, 48, None, None, None, 64, None, 96, 112, 128, 144, 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_block_backward_saved(F64, 16, 32, 48, None, None, None, 64, 80, 96, 112, 128, 144, 2, 2052, None) == TOO_MANY_STEPS
+    size = ctypes.c_size_t(7)
+    assert lib.cufkb_block_state_bytes(F32, 2, 3, ctypes.byref(size)) == POINT_COUNT and size.value == 0
+    assert lib.cufkb_block_state_bytes(F32, 0, 10, ctypes.byref(size)) == SUCCESS and size.value == 0
+    assert lib.cufkb_block_state_bytes(BF16, 5, 10, ctypes.byref(size)) == SUCCESS and size.value == 0
+    assert lib.cufkb_block_state_bytes(F32, 5, 10, None) == NULL_POINTER
 
 
 def test_torsion_validation(lib):

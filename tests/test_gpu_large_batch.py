@@ -1,6 +1,5 @@
-"""Large batches: float chains then run two per CTA on packed float2 lanes.  Odd batch sizes leave
-the last CTA with one chain.  Chains at the start, middle and end of the batch are checked against
-the float64 oracle."""
+"""Large (and odd) batch sizes through the public API, every dtype: chains at the start, middle and
+end of the batch are checked against the float64 oracle."""
 
 from __future__ import annotations
 
@@ -23,7 +22,7 @@ def _rows(b):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("batch,points", [(2049, 33), (1999, 768), (1185, 2051), (3001, 4)])
-def test_block_pairs(dtype, batch, points):
+def test_block_large_batch(dtype, batch, points):
     anchors = points != 4
     inp = nerf64.make_inputs(batch, points, seed=batch + points, anchors=anchors)
     L, A, D = (inp[k].to("cuda", dtype).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
@@ -43,7 +42,7 @@ def test_block_pairs(dtype, batch, points):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("batch,points", [(2049, 100), (1201, 2051)])
-def test_torsion_pairs(dtype, batch, points):
+def test_torsion_large_batch(dtype, batch, points):
     inp = nerf64.make_torsion_inputs(batch, points, seed=batch)
     f = cufk.compile_torsion(nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES)
     raw = inp["raw"].to("cuda", dtype).requires_grad_(True)
@@ -57,8 +56,8 @@ def test_torsion_pairs(dtype, batch, points):
     assert float((raw.grad[rows].double().cpu() - rg).norm() / rg.norm()) <= gt
 
 
-def test_pairs_match_singles_bitwise_per_chain():
-    # the same chain computed alone (one chain per CTA) and inside a large batch (two per CTA)
+def test_chain_result_does_not_depend_on_the_batch():
+    # a chain computed alone (the plan gives it more warps) and inside a large batch
     inp = nerf64.make_inputs(2400, 300, seed=5)
     L, A, D = (inp[k].cuda() for k in ("lengths", "angles", "dihedrals"))
     big = cufk.reconstruct(L, A, D)
