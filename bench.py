@@ -268,29 +268,29 @@ def run_ours(args, dist: Dist) -> dict | None:
         sets.append(d)
     torch.cuda.synchronize()
 
-    # The step is what cufk_b200.reconstruct + autograd runs: the forward that also writes the
-    # per-segment frames, then the backward that reads them and the forward's xyz.
+    # The step is what cufk_b200.reconstruct + autograd runs: the forward, then the backward that
+    # reads the forward's xyz (float32).
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     graphs_step, graphs_fwd, graphs_bwd = [], [], []
     with torch.cuda.stream(stream):
         for d in sets:  # eager warm-up of both kernels (first-call attribute setup happens here)
-            d["xyz"], d["state"] = C.block_forward_save(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-            C.block_backward_saved(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["state"], d["grad"])
+            d["xyz"] = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+            C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
         stream.synchronize()
         for d in sets:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                xyz, state = C.block_forward_save(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-                C.block_backward_saved(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, state, d["grad"])
+                xyz = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, d["grad"])
             graphs_step.append(g)
             gf = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gf, stream=stream):
-                C.block_forward_save(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
             graphs_fwd.append(gf)
             gb = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gb, stream=stream):
-                C.block_backward_saved(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["state"], d["grad"])
+                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
             graphs_bwd.append(gb)
     torch.cuda.synchronize()
 
@@ -310,12 +310,11 @@ def run_ours(args, dist: Dist) -> dict | None:
     atoms_local = b_local * n
     per_kernel = {
         "block_forward_kernel": (ms_fwd, fwd_bpa),
-        "block_backward_saved_kernel": (ms_bwd, bwd_bpa),
+        "block_backward_xyz_kernel": (ms_bwd, bwd_bpa),
     }
-    state_bpa = d["state"].numel() / (b_local * n)
-    # bytes the design actually moves: the forward also writes the frames, the backward also reads
-    # the forward's xyz and the frames
-    moved_bpa = {"block_forward_kernel": fwd_bpa + state_bpa, "block_backward_saved_kernel": bwd_bpa + 12.0 + state_bpa}
+    # bytes the kernels move: the backward reads the forward's xyz (3N) in place of the three input
+    # rows (3N - 6) and only three scalars of the inputs
+    moved_bpa = {"block_forward_kernel": fwd_bpa, "block_backward_xyz_kernel": (9 * n - 6) * 4 / n}
     dom = max(per_kernel, key=lambda k: per_kernel[k][0])
     ms_dom, bpa_dom = per_kernel[dom]
     achieved = bpa_dom * atoms_local / (ms_dom * 1e-3) / 1e9
@@ -399,7 +398,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "roofline": roofline,
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,
-        "kernels": "block_forward_kernel (writing the saved frames) + block_backward_saved_kernel per step",
+        "kernels": "block_forward_kernel + block_backward_xyz_kernel per step",
         "clocks": sampler.summary(),
     }
     if allgather is not None:

@@ -15,7 +15,7 @@ try:
     from . import _C  # noqa: E402
 except OSError as exc:  # pragma: no cover - exercised only on an unbuilt checkout
     raise ImportError(
-        f"cufk_b200 native library not built ({exc}); run `python -m cufk_b200.build` "
+        f"cufk_b200 native library not built ({exc}); run `python cufk_b200/build.py` "
         "(or __graft_entry__.build()) first"
     ) from exc
 

@@ -8,7 +8,8 @@
 Both are rebuilt only when a source is newer than the artefact (or with ``force``).  Nothing is
 written outside the package directory and its ``_build/`` folder.
 
-Usage: ``python -m cufk_b200.build [--force]``.
+Usage: ``python cufk_b200/build.py [--force]`` (run as a script, so that the package and its old
+native libraries are not imported before they are rebuilt).
 """
 
 from __future__ import annotations

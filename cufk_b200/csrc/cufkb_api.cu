@@ -214,31 +214,20 @@ constexpr int dtype_index() {
 }
 
 // Kernel ids for the caches: kind (5) x dtype (4).
-enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardSaved = 4 };
+enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardXyz = 4 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 template <typename T>
-using StateT = typename cufkb::ComputeOf<T>::type;
-
-// The forward's plan: the saved-state backward must use the same threads per chain and steps per
-// thread, so both compute it from the forward kernel's footprint.
-template <typename T>
-int block_forward_plan(int64_t batch, int points, LaunchEnv* env, size_t* smem) {
-  *smem = cufkb::block_smem_bytes<T>(points, false);
-  return launch_env(env, cufkb::block_forward_kernel<T>, kernel_id(kBlockForward, dtype_index<T>()), batch, points, *smem);
-}
-
-template <typename T>
-int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, void* state, int64_t batch,
-                       int points, cudaStream_t stream) {
+int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
+                       cudaStream_t stream) {
+  const size_t smem = cufkb::block_smem_bytes<T>(points, false);
+  auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
-  size_t smem;
-  if (int st = block_forward_plan<T>(batch, points, &env, &smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockForward, dtype_index<T>()), batch, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  cufkb::block_forward_kernel<T><<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz),
-                                                                                                   static_cast<StateT<T>*>(state), geo);
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
@@ -259,37 +248,20 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
   return CUFKB_SUCCESS;
 }
 
-// Saved-state backward (32- and 64-bit types): the forward's plan, its xyz and its state.
+// Backward from the forward's xyz (32- and 64-bit types).
 template <typename T>
-int block_backward_saved_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz,
-                              const void* state, const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
-  LaunchEnv fwd;
-  size_t fwd_smem;
-  if (int st = block_forward_plan<T>(batch, points, &fwd, &fwd_smem)) return st;
+int block_backward_xyz_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
+                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
-  auto kernel = cufkb::block_backward_saved_kernel<T>;
+  auto kernel = cufkb::block_backward_xyz_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardSaved, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardXyz, dtype_index<T>()), batch, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, fwd.plan.items};
-  kernel<<<static_cast<unsigned>(batch), fwd.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const StateT<T>*>(state),
-                                                                         static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
-                                                                         static_cast<T*>(gD), geo);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
-  return CUFKB_SUCCESS;
-}
-
-template <typename T>
-int block_state_bytes(int64_t batch, int points, size_t* bytes) {
-  *bytes = 0;
-  if constexpr (sizeof(T) >= 4) {
-    if (batch == 0) return CUFKB_SUCCESS;
-    LaunchEnv env;
-    size_t smem;
-    if (int st = block_forward_plan<T>(batch, points, &env, &smem)) return st;
-    *bytes = static_cast<size_t>(batch) * env.plan.threads * cufkb::kStateWords * sizeof(StateT<T>);
-  }
   return CUFKB_SUCCESS;
 }
 
@@ -348,8 +320,8 @@ int check_block_pointers(int dtype, std::initializer_list<const void*> required,
   return CUFKB_SUCCESS;
 }
 
-int block_forward_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, void* state,
-                           int64_t batch, int64_t points, cufkb_stream_t stream) {
+int block_forward_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
+                           int64_t points, cufkb_stream_t stream) {
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
   if (int st = check_block_pointers(dtype, {L, A, D, xyz}, {L, A, D, p0, fd, nn, xyz})) return st;
@@ -357,13 +329,13 @@ int block_forward_dispatch(int dtype, const void* L, const void* A, const void* 
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, state, batch, n, s);
+      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, batch, n, s);
     case CUFKB_FLOAT64:
-      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, state, batch, n, s);
+      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, batch, n, s);
     case CUFKB_FLOAT16:
-      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, nullptr, batch, n, s);
+      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s);
     default:
-      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, nullptr, batch, n, s);
+      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s);
   }
 }
 
@@ -375,29 +347,7 @@ int cufkb_max_point_count(void) { return CUFKB_MAX_POINT_COUNT; }
 
 int cufkb_block_forward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                         const void* initial_normal, void* xyz, int64_t batch, int64_t points, cufkb_stream_t stream) {
-  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, nullptr, batch, points, stream);
-}
-
-int cufkb_block_state_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes) {
-  if (!bytes) return CUFKB_ERROR_NULL_POINTER;
-  *bytes = 0;
-  if (int st = check_shape(dtype, batch, points)) return st;
-  const int n = static_cast<int>(points);
-  switch (dtype) {
-    case CUFKB_FLOAT32:
-      return block_state_bytes<float>(batch, n, bytes);
-    case CUFKB_FLOAT64:
-      return block_state_bytes<double>(batch, n, bytes);
-    default:
-      return CUFKB_SUCCESS;
-  }
-}
-
-int cufkb_block_forward_save(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
-                             const void* initial_normal, void* xyz, void* state, int64_t batch, int64_t points, cufkb_stream_t stream) {
-  if ((dtype == CUFKB_FLOAT32 || dtype == CUFKB_FLOAT64) && batch > 0 && state == nullptr) return CUFKB_ERROR_NULL_POINTER;
-  if (!aligned(state, 16)) return CUFKB_ERROR_MISALIGNED;
-  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, batch, points, stream);
+  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, points, stream);
 }
 
 int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
@@ -428,29 +378,30 @@ int cufkb_block_backward(int dtype, const void* lengths, const void* angles, con
   }
 }
 
-int cufkb_block_backward_saved(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
-                               const void* initial_normal, const void* xyz, const void* state, const void* grad_xyz, void* grad_lengths,
-                               void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
+int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                                  const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
+                                  void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
   if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
+    if (int st = check_shape(dtype, batch, points)) return st;
+    if (batch > 0 && !xyz) return CUFKB_ERROR_NULL_POINTER;
     return cufkb_block_backward(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
                                 grad_dihedrals, batch, points, stream);
   }
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
-  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, state, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
                                     {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
                                      grad_dihedrals})) {
     return st;
   }
-  if (!aligned(state, 16)) return CUFKB_ERROR_MISALIGNED;
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == CUFKB_FLOAT32) {
-    return block_backward_saved_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, grad_xyz, grad_lengths,
-                                            grad_angles, grad_dihedrals, batch, n, s);
+    return block_backward_xyz_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                          grad_dihedrals, batch, n, s);
   }
-  return block_backward_saved_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, state, grad_xyz, grad_lengths, grad_angles,
-                                           grad_dihedrals, batch, n, s);
+  return block_backward_xyz_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s);
 }
 
 int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,

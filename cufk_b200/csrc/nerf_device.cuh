@@ -94,6 +94,9 @@ __device__ __forceinline__ float vadd(float a, float b) { return a + b; }
 __device__ __forceinline__ double vadd(double a, double b) { return a + b; }
 __device__ __forceinline__ float vneg(float a) { return -a; }
 __device__ __forceinline__ double vneg(double a) { return -a; }
+// 1/sqrt(x): the CUDA math library's rsqrtf (float) and rsqrt (double)
+__device__ __forceinline__ float vrsqrt(float a) { return rsqrtf(a); }
+__device__ __forceinline__ double vrsqrt(double a) { return rsqrt(a); }
 // a - b
 __device__ __forceinline__ float vsub(float a, float b) { return a - b; }
 __device__ __forceinline__ double vsub(double a, double b) { return a - b; }
@@ -525,9 +528,5 @@ struct ChainGeometry {
   int steps;   // N - 3
   int items;   // K: steps per thread (odd)
 };
-
-// Saved state of one chain for the backward: the world frame (rotation row-major, then translation)
-// in front of each thread's first step, written by the forward that computed it.
-constexpr int kStateWords = 12;
 
 }  // namespace cufkb

@@ -2,7 +2,7 @@
 //
 // block_forward_kernel          <- src/cufk/csrc/block.cu:157-204   (xyz from lengths/angles/dihedrals)
 // block_backward_kernel         <- src/cufk/csrc/block.cu:206-313   (d lengths/angles/dihedrals)
-// block_backward_saved_kernel      the same gradients from the forward's xyz and saved frames
+// block_backward_xyz_kernel        the same gradients from the forward's xyz (no local transforms)
 // torsion_forward_kernel        <- src/cufk/csrc/torsion.cu:254-295 (xyz from raw (sin, cos) pairs)
 // torsion_backward_kernel       <- src/cufk/csrc/torsion.cu:297-381 (d raw pairs)
 //
@@ -12,8 +12,7 @@
 // Forward: stage the chain's inputs into atom slots (LDGSTS), sweep each thread's K steps
 // sequentially from the identity (the local prefix position written back into the slot), exclusive
 // affine scan of the thread totals across the CTA, then x = p2 + F (C.v + C.m v) per slot in place
-// and one bulk (TMA-engine) store of the (N, 3) row.  On request each thread also writes its world
-// frame (p2, F) C to a small state buffer (12 words per K steps).
+// and one bulk (TMA-engine) store of the (N, 3) row.
 //
 // Backward: the gradient of every parameter of step s follows from the force/moment suffix of the
 // atoms it moves.  In world coordinates (P_s = (F, p2) L_0...L_s, x = P.v):
@@ -28,9 +27,8 @@
 //   * Recompute form (block_backward_kernel, nothing saved): sweep 1 builds each thread's local
 //     prefix, its sum of g and the 3x3 moment matrix Q = sum p (x) g (p = local position), so that
 //     once the affine scan gives the thread's carry C its moment total is C.v x G + axial(C.m Q).
-//   * Saved form (block_backward_saved_kernel): the thread sums of g and x x g come straight from
-//     the forward's xyz and the carry from the saved state, so the chain is walked once instead of
-//     twice.
+//   * xyz form (block_backward_xyz_kernel): the frame columns the formulas need are bond
+//     directions and plane normals of the forward's xyz, so nothing is rebuilt from the inputs.
 //   Either way an exclusive suffix scan of the thread sums gives each thread the sums of all later
 //   threads, and sweep 2 recomputes the prefix from the carry, walks the running suffix down and
 //   writes the gradients into the slots in place.
@@ -63,14 +61,26 @@ struct CtaExchange {
   Affine<V> warp_totals[kMaxWarps];
   V warp_sums[kMaxWarps * 6];  // suffix scan of (force, moment)
   V warp_red[kMaxWarps];       // first-frame reduction (separate: warps may still read warp_sums)
+  V frame[12];                 // base frame F (row-major) and p2, built once by thread 0
+  int general;                 // backward: base frame not orthonormal (set by thread 0)
 };
+
+// The chain's first frame from its anchors and (lengths[0], lengths[1], angles[0]), read from
+// global memory (one thread per CTA builds it; the staged rows are still in flight).
+template <typename T, typename V>
+__device__ __forceinline__ ChainFrame<V> chain_frame_of(const BlockArgs<T>& args, const AnchorFrame<V>& af, int64_t chain, int N) {
+  const V l0 = to_r<V>(args.lengths[chain * (N - 1)]);
+  const V l1 = to_r<V>(args.lengths[chain * (N - 1) + 1]);
+  const V a0 = to_r<V>(args.angles[chain * (N - 2)]);
+  return chain_frame<V>(af, l0, l1, a0);
+}
 
 // --------------------------------------------------------------------------------------------
 // shared-memory layout of one chain
 // --------------------------------------------------------------------------------------------
 // 4- and 8-byte types ("scatter"): [X slots, 3N elements of T, offset so that X has the residue of
-//   the output row mod 16] [G staged grad row (backward)]; the saved backward stages the forward's
-//   xyz into the slot row before the inputs (see block_backward_saved_kernel)
+//   the output row mod 16] [G staged grad row (backward)]; the xyz backward stages the forward's
+//   xyz row where the slots would be
 // 16-bit types: [X slots, 3N floats] [staged input rows (T)] [G staged grad row (backward)]
 __host__ __device__ inline size_t slot_bytes(int points, size_t elem) { return staged_row_bytes(size_t(3) * points, elem); }
 
@@ -113,7 +123,7 @@ struct ChainViews {
   R* X;               // atom slots
   const T* row[3];    // staged input rows of 16-bit types (lengths/angles/dihedrals or raw pairs)
   T* G;               // staged gradient row (backward)
-  const T* Y;         // staged xyz row of the forward (saved backward)
+  const T* Y;         // staged xyz row of the forward (xyz backward)
 
   __device__ __forceinline__ R slot(int off) const { return X[off]; }
   __device__ __forceinline__ void set_slot(int off, R v) const { X[off] = v; }
@@ -385,6 +395,12 @@ struct BackwardFrame {
   bool general;    // base frame not orthonormal: use base coordinates
 };
 
+template <typename V>
+struct FirstFrame {
+  AnchorFrame<V> af;
+  BackwardFrame<V> bf;
+};
+
 template <typename V, typename S>
 __device__ __forceinline__ BackwardFrame<V> backward_frame(const AnchorFrame<S>& af, V l0, V l1, V a0) {
   BackwardFrame<V> b;
@@ -404,9 +420,9 @@ __device__ __forceinline__ BackwardFrame<V> backward_frame(const AnchorFrame<S>&
 
 // Gradients of lengths[0], lengths[1] and angles[0] (write_first_frame_param_grads,
 // block.cu:206-228) into atom slots 1 and 2, by thread 0.  F3 and M3 are the suffix sums over every
-// atom >= 3 (world coordinates) or F3 in base coordinates and `acc` the reduced first-frame term
-// (base coordinates).
-template <bool kWorld, typename T, typename V>
+// atom >= 3 (world coordinates; kAboutP2: moments taken about p2) or F3 in base coordinates and
+// `acc` the reduced first-frame term (base coordinates).
+template <bool kWorld, typename T, typename V, bool kAboutP2 = false>
 __device__ __forceinline__ void first_frame_grads(const ChainViews<T>& cv, const AnchorFrame<V>& af, const BackwardFrame<V>& bf, const T* grow, const V* F3,
                                                   const V* M3, V acc) {
   const ChainFrame<V>& ff = bf.ff;
@@ -420,10 +436,14 @@ __device__ __forceinline__ void first_frame_grads(const ChainViews<T>& cv, const
   }
   if constexpr (kWorld) {
     // the z moment about p2 in base coordinates is normal . (M3 - p2 x F3); for an orthonormal frame
-    // the first-frame projection term is -bv[0] times it
-    V pf[3];
-    cross3(ff.p2, F3, pf);
-    const V m_about_p2[3] = {vsub(M3[0], pf[0]), vsub(M3[1], pf[1]), vsub(M3[2], pf[2])};
+    // the first-frame projection term is -bv[0] times it.  With kAboutP2, M3 is already about p2.
+    V m_about_p2[3] = {M3[0], M3[1], M3[2]};
+    if constexpr (!kAboutP2) {
+      V pf[3];
+      cross3(ff.p2, F3, pf);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) m_about_p2[i] = vsub(M3[i], pf[i]);
+    }
     acc = vneg(vmul(bf.bv[0], dot3(ff.normal, m_about_p2)));
 #pragma unroll
     for (int i = 0; i < 3; ++i) grad_p2[i] = vadd(g2[i], F3[i]);
@@ -488,7 +508,7 @@ __device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* gr
 // --------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
-    block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, typename ComputeOf<T>::type* __restrict__ state, ChainGeometry geo) {
+    block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo) {
   using R = typename ComputeOf<T>::type;
   using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
@@ -501,28 +521,27 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   T* out = xyz + chain * 3 * N;
   ChainViews<T> cv;
   stage_block_inputs<T>(cv, smem, args, chain, N, kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : 0, tid, nthr);
-  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+  // thread 0 builds the first frame while the rows stage; the others read (F, p2) after the scan
+  V first_points[9];
+  if (tid == 0) {
+    const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+    const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, chain, N);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) ex.frame[i] = ff.F[i];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      ex.frame[9 + i] = ff.p2[i];
+      first_points[i] = af.p0[i];
+      first_points[3 + i] = ff.p1[i];
+      first_points[6 + i] = ff.p2[i];
+    }
+  }
   cp_async_wait_all();
   __syncthreads();
-
-  V F[9], p2[3];
-  {
-    V l0, l1, a0;
-    first_inputs(cv, l0, l1, a0);
-    const ChainFrame<V> ff = chain_frame<V>(af, l0, l1, a0);
+  if (tid == 0) {
+    // atoms 0..2; their slots held lengths[0..1] and angles[0], which nothing else reads
 #pragma unroll
-    for (int i = 0; i < 9; ++i) F[i] = ff.F[i];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) p2[i] = ff.p2[i];
-    if constexpr (kScatter) __syncthreads();  // every thread has read l0, l1, a0 from atom slots 1, 2
-    if (tid == 0) {
-#pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        cv.set_slot(i, af.p0[i]);
-        cv.set_slot(3 + i, ff.p1[i]);
-        cv.set_slot(6 + i, ff.p2[i]);
-      }
-    }
+    for (int i = 0; i < 9; ++i) cv.set_slot(i, first_points[i]);
   }
 
   auto step = [&](int s) {
@@ -534,15 +553,9 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
 
   const StepRange range = step_range(tid, K, St);
   const Affine<V> total = sweep_local_prefix<T, V>(cv, range, step);
-  const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
+  // ex.frame was written before the barrier that follows the staging
+  const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), ex.frame, ex.frame + 9);
   apply_carry<T, V>(cv, W, range);
-  if (state != nullptr) {
-    R* dst = state + (chain * nthr + tid) * kStateWords;
-#pragma unroll
-    for (int i = 0; i < 9; ++i) dst[i] = W.m[i];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) dst[9 + i] = W.v[i];
-  }
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 
@@ -584,19 +597,27 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
   write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);
 }
 
-// Backward from the forward's xyz and saved state (4- and 8-byte types; the launch plan must be the
-// forward's).  Shared memory holds two rows: the staged gradient row G and a slot row that first
-// receives the forward's xyz (for the thread sums of g and x x g) and then the scattered inputs (for
-// sweep 2), whose loads overlap the suffix scan.  A chain whose base frame is not orthonormal
-// falls back to the recompute form.
+// Backward from the forward's xyz (4- and 8-byte types, base frame orthonormal).  In world
+// coordinates every gradient of step s needs only the positions around it and the suffix sums
+// F_s = sum_{j >= s+3} g_j, M_s = sum_{j >= s+3} (x_j - o) x g_j (moments about the chain's own
+// p2 = o, so that tau keeps its precision however far the chain is from the world origin):
+//   u_b = (x_{b+1} - x_b) / |x_{b+1} - x_b|          (bond b; u_{s+1} = P_{s-1}.col0, u_{s+2} = P_s.col0)
+//   P_s.col2 = (u_{s+1} x u_{s+2}) / sin(theta_s)    (the frame normal; |u_{s+1} x u_{s+2}| = sin theta_s)
+// so no local transform is rebuilt: the chain's xyz and grad rows are staged (16-byte LDGSTS), each
+// thread sums g and (x - o) x g over its atoms, an exclusive suffix scan gives the sums of all later
+// threads, and one sweep up the thread's steps produces the three gradients, written over the
+// grad row in place (step s only reads g_{s+3}, its own atom).  A chain is redone by the recompute
+// form in the same CTA when its base frame is not orthonormal, when a bond is shorter than
+// 1e-3 |x|max (its direction from rounded positions would be off by more than ~1e-4: a zero-length
+// bond, or a chain far from the origin relative to its bond lengths), when a plane normal has
+// sin^2 theta < 1e-2 (bond angle within ~6 degrees of 0 or pi), or when a value is not finite.
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
-    block_backward_saved_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const typename ComputeOf<T>::type* __restrict__ state,
-                                const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths, T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals,
-                                ChainGeometry geo) {
+    block_backward_xyz_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
+                              T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
   using R = typename ComputeOf<T>::type;
   using V = R;
-  static_assert(sizeof(T) >= 4, "the saved form serves 32- and 64-bit types");
+  static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
@@ -604,51 +625,42 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   const int64_t chain = blockIdx.x;
   const T* grow = grad_xyz + chain * 3 * N;
+  unsigned char* const slot_region = smem;
+  unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
   ChainViews<T> cv;
-  unsigned char* slot_region = smem;
-  cv.X = reinterpret_cast<R*>(slot_region);
-  cv.G = stage_row_async(smem + slot_bytes(N, sizeof(R)), grow, 3 * N, tid, nthr);
   cv.Y = stage_row_async(slot_region, xyz + chain * 3 * N, 3 * N, tid, nthr);
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
-  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-  const R l0 = args.lengths[chain * (N - 1)];
-  const R l1 = args.lengths[chain * (N - 1) + 1];
-  const R a0 = args.angles[chain * (N - 2)];
-  const BackwardFrame<V> bf = backward_frame<V>(af, l0, l1, a0);
-  auto step = [&](int s) {
-    V l, th, ph, st, ct, sp, cp;
-    block_step_inputs<T>(cv, s, l, th, ph);
-    step_sincos(th, ph, st, ct, sp, cp);
-    return step_rot(l, st, ct, sp, cp);
+  cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
+  cv.X = cv.G;  // gradients go over the consumed grad row
+  // thread 0 classifies the base frame while the rows stage; the first frame itself is only needed
+  // again by thread 0 for the first-frame gradients (and by the recompute form)
+  auto first_frame = [&]() {
+    const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+    const R l0 = to_r<R>(args.lengths[chain * (N - 1)]);
+    const R l1 = to_r<R>(args.lengths[chain * (N - 1) + 1]);
+    const R a0 = to_r<R>(args.angles[chain * (N - 2)]);
+    return FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
   };
+  if (tid == 0) ex.general = first_frame().bf.general ? 1 : 0;
   const StepRange range = step_range(tid, K, St);
-  if (bf.general) {
-    // recompute form: inputs into the slots, gradients staged as for block_backward_kernel
-    cp_async_wait_all();
-    __syncthreads();
-    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
-    cp_async_wait_all();
-    __syncthreads();
-    block_backward_general<T, V>(cv, ex, af, bf, grow, range, nwarps, step);
-  } else {
-    Affine<V> carry;
-    {
-      const R* src = state + (chain * nthr + tid) * kStateWords;
-#pragma unroll
-      for (int i = 0; i < 9; ++i) carry.m[i] = src[i];
-#pragma unroll
-      for (int i = 0; i < 3; ++i) carry.v[i] = src[9 + i];
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    // thread sums of g and x x g straight from the staged rows
+  cp_async_wait_all();
+  __syncthreads();
+
+  const bool general = ex.general != 0;  // uniform over the CTA
+  bool redo = general;
+  if (!redo) {
+    // moments about o = p2 (the chain's own origin, atom 2 of the forward's xyz): tau then loses no
+    // precision to the chain's distance from the world origin
+    const V o[3] = {cv.pos(6), cv.pos(7), cv.pos(8)};
     V gsum[3] = {V(0), V(0), V(0)};
     V msum[3] = {V(0), V(0), V(0)};
+    V xmax2 = V(0);  // largest |x|^2 of the thread's atoms (world), for the short-bond test
     int off = 3 * (range.first + 3);
 #pragma unroll 4
     for (int k = 0; k < range.count; ++k, off += 3) {
       const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
-      const V x[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+      const V xw[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+      xmax2 = fmax(xmax2, dot3(xw, xw));
+      const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
       V mx[3];
       cross3(x, g, mx);
 #pragma unroll
@@ -657,16 +669,93 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
         msum[i] = vadd(msum[i], mx[i]);
       }
     }
-    __syncthreads();  // the xyz row is consumed: the slot row now takes the inputs
-    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
     V Fs[3], Ms[3];
     suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
     const V F3[3] = {Fs[0], Fs[1], Fs[2]};
     const V M3[3] = {Ms[0], Ms[1], Ms[2]};
+    // sweep: x2 = x_{s+2} (world), up = u_{s+1} carried from step to step.  Threads without steps
+    // read nothing (their first step lies past the chain).
+    V x2[3] = {V(0), V(0), V(0)};
+    V up[3] = {V(0), V(0), V(0)};
+    V dmin2 = V(0);
+    if (range.count > 0) {
+      off = 3 * (range.first + 1);  // atoms first+1 and first+2 <= N-2
+#pragma unroll
+      for (int i = 0; i < 3; ++i) x2[i] = cv.pos(off + 3 + i);
+      const V d[3] = {vsub(x2[0], cv.pos(off)), vsub(x2[1], cv.pos(off + 1)), vsub(x2[2], cv.pos(off + 2))};
+      dmin2 = dot3(d, d);
+      xmax2 = fmax(xmax2, dot3(x2, x2));
+      const V inv = vrsqrt(dmin2);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) up[i] = vmul(d[i], inv);
+    }
+    V wmin2 = V(1);
+    off = 3 * (range.first + 3);
+#pragma unroll 2
+    for (int k = 0; k < range.count; ++k, off += 3) {
+      const V x3[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+      const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+      const V d[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+      const V d2 = dot3(d, d);
+      dmin2 = fmin(dmin2, d2);
+      const V inv = vrsqrt(d2);
+      const V uc[3] = {vmul(d[0], inv), vmul(d[1], inv), vmul(d[2], inv)};
+      const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+      V xf[3];
+      cross3(xr, Fs, xf);
+      const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
+      V w[3];
+      cross3(up, uc, w);
+      const V w2 = dot3(w, w);
+      wmin2 = fmin(wmin2, w2);
+      const V d_phi = dot3(up, tau);
+      const V d_len = dot3(uc, Fs);
+      const V d_theta = vneg(vmul(dot3(w, tau), vrsqrt(w2)));
+      const V x3r[3] = {vsub(x3[0], o[0]), vsub(x3[1], o[1]), vsub(x3[2], o[2])};
+      V mx[3];
+      cross3(x3r, g, mx);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        Fs[i] = vsub(Fs[i], g[i]);
+        Ms[i] = vsub(Ms[i], mx[i]);
+        x2[i] = x3[i];
+        up[i] = uc[i];
+      }
+      cv.set_slot(off, d_len);
+      cv.set_slot(off + 1, d_theta);
+      cv.set_slot(off + 2, d_phi);
+    }
+    // Positions are accurate to ~1 ulp of |x|, so a bond direction from them is good to
+    // ~ulp(|x|) / |d|: bonds shorter than 1e-3 |x|max, a plane normal with sin^2 < 1e-2 (and any
+    // non-finite value: the comparisons fail) send the chain to the recompute form.
+    const bool bad = range.count > 0 && !(dmin2 >= static_cast<V>(1e-6) * xmax2 && wmin2 >= static_cast<V>(1e-2));
+    redo = __syncthreads_or(bad) != 0;
+    if (!redo && tid == 0) {
+      const FirstFrame<V> f = first_frame();
+      first_frame_grads<true, T, V, true>(cv, f.af, f.bf, grow, F3, M3, V(0));
+    }
+  }
+  if (redo) {
+    const FirstFrame<V> f = first_frame();
+    const AnchorFrame<V>& af = f.af;
+    const BackwardFrame<V>& bf = f.bf;
+    // recompute form, laid out as in block_backward_kernel: inputs into the slots, grad row restaged
+    __syncthreads();
+    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
+    cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
     cp_async_wait_all();
     __syncthreads();
-    block_backward_sweep2<true, T, V>(cv, bf.ff.F, carry, Fs, Ms, bf.av, bf.bv, range, step);
-    if (tid == 0) first_frame_grads<true, T, V>(cv, af, bf, grow, F3, M3, V(0));
+    auto step = [&](int s) {
+      V l, th, ph, st, ct, sp, cp;
+      block_step_inputs<T>(cv, s, l, th, ph);
+      step_sincos(th, ph, st, ct, sp, cp);
+      return step_rot(l, st, ct, sp, cp);
+    };
+    if (general) {
+      block_backward_general<T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+    } else {
+      block_backward_recompute<true, T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+    }
   }
   __syncthreads();
   write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);

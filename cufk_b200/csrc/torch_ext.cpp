@@ -149,33 +149,17 @@ Tensor block_forward_impl(const Tensor& lengths, const Tensor& angles, const Ten
   return xyz;
 }
 
-// Forward that also returns the per-segment frames the saved backward reads (an empty tensor for the
-// 16-bit types, whose backward recomputes).
-std::vector<Tensor> block_forward_save_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a,
-                                            const Shape& shape) {
-  const c10::cuda::CUDAGuard guard(lengths.device());
-  const int dtype = dtype_code(lengths.scalar_type());
-  size_t bytes = 0;
-  check_status(cufkb_block_state_bytes(dtype, shape.batch, shape.points, &bytes), "reconstruct");
-  Tensor xyz = torch::empty({shape.batch, shape.points, 3}, lengths.options());
-  Tensor state = torch::empty({static_cast<int64_t>(bytes)}, lengths.options().dtype(torch::kUInt8));
-  check_status(cufkb_block_forward_save(dtype, lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(), ptr_or_null(a.p0),
-                                        ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
-                                        bytes ? state.data_ptr() : nullptr, shape.batch, shape.points, current_stream()),
-               "reconstruct");
-  return {xyz, state};
-}
-
-std::vector<Tensor> block_backward_saved_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a,
-                                              const Tensor& xyz, const Tensor& state, const Tensor& grad_points, const Shape& shape) {
+// Backward from the forward's output xyz (float32/float64; 16-bit types recompute).
+std::vector<Tensor> block_backward_xyz_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Tensor& xyz,
+                                            const Tensor& grad_points, const Shape& shape) {
   const c10::cuda::CUDAGuard guard(lengths.device());
   Tensor gl = torch::empty_like(lengths);
   Tensor ga = torch::empty_like(angles);
   Tensor gd = torch::empty_like(dihedrals);
-  check_status(cufkb_block_backward_saved(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
-                                          ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
-                                          state.numel() ? state.data_ptr() : nullptr, grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(),
-                                          gd.data_ptr(), shape.batch, shape.points, current_stream()),
+  check_status(cufkb_block_backward_from_xyz(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                             ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
+                                             grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(), shape.batch, shape.points,
+                                             current_stream()),
                "reconstruct backward");
   return {gl, ga, gd};
 }
@@ -205,11 +189,10 @@ class ReconstructAutograd : public torch::autograd::Function<ReconstructAutograd
                         std::optional<Tensor> first_direction, std::optional<Tensor> initial_normal) {
     const Shape shape = check_geom(lengths, angles, dihedrals);
     const Anchors a = checked_anchors(opt(p0), opt(first_direction), opt(initial_normal), lengths, shape);
-    // the saved backward reads the output and the per-segment frames instead of walking the chain
-    // a second time; the version counter of the saved output catches in-place edits of xyz
-    auto out = block_forward_save_impl(lengths, angles, dihedrals, a, shape);
-    Tensor xyz = out[0];
-    ctx->save_for_backward({lengths, angles, dihedrals, xyz, out[1]});
+    // the backward reads the output instead of walking the chain again; the version counter of the
+    // saved output catches in-place edits of xyz
+    Tensor xyz = block_forward_impl(lengths, angles, dihedrals, a, shape);
+    ctx->save_for_backward({lengths, angles, dihedrals, xyz});
     ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
     ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
     ctx->saved_data["initial_normal"] = a.initial_normal.defined() ? c10::IValue(a.initial_normal) : c10::IValue();
@@ -229,7 +212,7 @@ class ReconstructAutograd : public torch::autograd::Function<ReconstructAutograd
       return v.isTensor() ? v.toTensor() : Tensor();
     };
     const Anchors a{anchor("p0"), anchor("first_direction"), anchor("initial_normal")};
-    auto grads = block_backward_saved_impl(lengths, angles, dihedrals, a, saved[3], saved[4], grad_points, shape);
+    auto grads = block_backward_xyz_impl(lengths, angles, dihedrals, a, saved[3], grad_points, shape);
     return {grads[0], grads[1], grads[2], Tensor(), Tensor(), Tensor()};
   }
 };
@@ -319,30 +302,16 @@ std::vector<Tensor> block_backward(const Tensor& lengths, const Tensor& angles, 
   return block_backward_impl(lengths, angles, dihedrals, a, grad_points, shape);
 }
 
-std::vector<Tensor> block_forward_save(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
-                                       const std::optional<Tensor>& fd, const std::optional<Tensor>& nn) {
-  const Shape shape = check_geom(lengths, angles, dihedrals);
-  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
-  return block_forward_save_impl(lengths, angles, dihedrals, a, shape);
-}
-
-std::vector<Tensor> block_backward_saved(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
-                                         const std::optional<Tensor>& fd, const std::optional<Tensor>& nn, const Tensor& xyz, const Tensor& state,
-                                         const Tensor& grad_points) {
+std::vector<Tensor> block_backward_from_xyz(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                                            const std::optional<Tensor>& fd, const std::optional<Tensor>& nn, const Tensor& xyz,
+                                            const Tensor& grad_points) {
   const Shape shape = check_geom(lengths, angles, dihedrals);
   const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
   check_like(grad_points, lengths, "grad_points");
   check_like(xyz, lengths, "xyz");
   TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
   TORCH_CHECK(xyz.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "xyz must have shape (B, N, 3)");
-  TORCH_CHECK(state.is_cuda() && state.scalar_type() == torch::kUInt8 && state.is_contiguous(), "state must be the uint8 tensor of block_forward_save");
-  size_t bytes = 0;
-  {
-    const c10::cuda::CUDAGuard guard(lengths.device());
-    check_status(cufkb_block_state_bytes(dtype_code(lengths.scalar_type()), shape.batch, shape.points, &bytes), "reconstruct backward");
-  }
-  TORCH_CHECK(static_cast<size_t>(state.numel()) == bytes, "state does not match these sizes (", state.numel(), " bytes, expected ", bytes, ")");
-  return block_backward_saved_impl(lengths, angles, dihedrals, a, xyz, state, grad_points, shape);
+  return block_backward_xyz_impl(lengths, angles, dihedrals, a, xyz, grad_points, shape);
 }
 
 Tensor torsion_forward(const Tensor& raw, const std::vector<double>& consts) { return torsion_forward_impl(raw, consts, check_pairs(raw)); }
@@ -367,12 +336,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("block_backward", &block_backward, "backward kernel only", pybind11::arg("lengths"), pybind11::arg("angles"),
         pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
         pybind11::arg("grad_points"));
-  m.def("block_forward_save", &block_forward_save, "forward kernel writing the saved-backward state", pybind11::arg("lengths"),
-        pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
-        pybind11::arg("initial_normal") = pybind11::none());
-  m.def("block_backward_saved", &block_backward_saved, "backward kernel from the forward's xyz and state", pybind11::arg("lengths"),
+  m.def("block_backward_from_xyz", &block_backward_from_xyz, "backward kernel reading the forward's xyz", pybind11::arg("lengths"),
         pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
-        pybind11::arg("xyz"), pybind11::arg("state"), pybind11::arg("grad_points"));
+        pybind11::arg("xyz"), pybind11::arg("grad_points"));
   m.def("torsion_forward", &torsion_forward, "torsion forward kernel only");
   m.def("torsion_backward", &torsion_backward, "torsion backward kernel only");
   m.def("max_point_count", &cufkb_max_point_count);

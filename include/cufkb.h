@@ -19,6 +19,7 @@
  *   cufkb_block_forward   <- forward_cuda_impl<T>   src/cufk/csrc/block.cu:319-329
  *                            (reached from _C.apply, block.cu:431-445 / _C.pyi:3-10)
  *   cufkb_block_backward  <- backward_cuda_impl<T>  src/cufk/csrc/block.cu:331-365
+ *   cufkb_block_backward_from_xyz <- backward_cuda_impl<T> as well (same gradients, reads xyz)
  *   cufkb_torsion_forward <- forward_default_impl<T> src/cufk/csrc/torsion.cu:387-397
  *   cufkb_torsion_backward<- backward_xyz_impl<T>   src/cufk/csrc/torsion.cu:399-411
  *   validation codes      <- TORCH_CHECKs of src/cufk/csrc/extension_utils.cuh:57-143
@@ -84,30 +85,23 @@ CUFKB_API int cufkb_block_forward(int dtype, const void* lengths, const void* an
                         const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
                         cufkb_stream_t stream);
 
-/* Bytes of the state cufkb_block_forward_save writes for these sizes on the current device (0 for
- * float16/bfloat16, whose backward always recomputes).  Needs the CUDA device. */
-CUFKB_API int cufkb_block_state_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes);
-
-/* cufkb_block_forward that also writes the per-segment world frames a later
- * cufkb_block_backward_saved needs (state: cufkb_block_state_bytes bytes, 16-byte aligned, device
- * memory).  No counterpart in the reference, whose backward always recomputes the chain. */
-CUFKB_API int cufkb_block_forward_save(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
-                             const void* first_direction, const void* initial_normal, void* xyz, void* state, int64_t batch,
-                             int64_t points, cufkb_stream_t stream);
-
 /* Gradients of sum(grad_xyz * xyz) w.r.t. lengths, angles and dihedrals (no anchor gradients).
  * Recomputes the forward prefix; needs nothing saved from cufkb_block_forward. */
 CUFKB_API int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                          const void* first_direction, const void* initial_normal, const void* grad_xyz, void* grad_lengths,
                          void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream);
 
-/* The same gradients as cufkb_block_backward from the xyz and state of a cufkb_block_forward_save
- * call with identical arguments on the same device: the chain is walked once instead of twice.
- * float16/bfloat16 ignore xyz and state and recompute.  Replaces backward_cuda_impl<T> as well. */
-CUFKB_API int cufkb_block_backward_saved(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
-                               const void* first_direction, const void* initial_normal, const void* xyz, const void* state,
-                               const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
-                               int64_t points, cufkb_stream_t stream);
+/* The same gradients as cufkb_block_backward, from xyz = the output of cufkb_block_forward with
+ * identical arguments: for an orthonormal base frame every gradient follows from the bond
+ * directions and plane normals of xyz and the running sums of grad_xyz, so the chain is not
+ * rebuilt.  Chains whose base frame is not orthonormal, or with a bond angle within ~6 degrees of 0
+ * or pi, are recomputed as cufkb_block_backward does.  float16/bfloat16 ignore xyz (a 16-bit
+ * position is too coarse for a bond direction) and recompute.  Replaces backward_cuda_impl<T> as
+ * well; the reference's backward always recomputes the chain. */
+CUFKB_API int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                  const void* first_direction, const void* initial_normal, const void* xyz, const void* grad_xyz,
+                                  void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
+                                  cufkb_stream_t stream);
 
 /* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
  * elements (any stride >= 0, pairs within a row contiguous). */

@@ -89,21 +89,17 @@ def test_block_backward_validation(lib):
     assert bwd(gl=82) == MISALIGNED
 
 
-def test_saved_path_validation(lib):
+def test_from_xyz_validation(lib):
     vp, i64 = ctypes.c_void_p, ctypes.c_int64
-    lib.cufkb_block_forward_save.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
-    lib.cufkb_block_backward_saved.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
-    lib.cufkb_block_state_bytes.argtypes = [ctypes.c_int, i64, i64, ctypes.POINTER(ctypes.c_size_t)]
-    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, None, 2, 10, None) == NULL_POINTER
-    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, 72, 2, 10, None) == MISALIGNED
-    assert lib.cufkb_block_forward_save(F32, 16, 32, 48, None, None, None, 64, 80, 2, 3, None) == POINT_COUNT
-    assert lib.cufkb_block_backward_saved(F32, 16, 32, 48, None, None, None, 64, None, 96, 112, 128, 144, 2, 10, None) == NULL_POINTER
-    assert lib.cufkb_block_backward_saved(F64, 16, 32, 48, None, None, None, 64, 80, 96, 112, 128, 144, 2, 2052, None) == TOO_MANY_STEPS
-    size = ctypes.c_size_t(7)
-    assert lib.cufkb_block_state_bytes(F32, 2, 3, ctypes.byref(size)) == POINT_COUNT and size.value == 0
-    assert lib.cufkb_block_state_bytes(F32, 0, 10, ctypes.byref(size)) == SUCCESS and size.value == 0
-    assert lib.cufkb_block_state_bytes(BF16, 5, 10, ctypes.byref(size)) == SUCCESS and size.value == 0
-    assert lib.cufkb_block_state_bytes(F32, 5, 10, None) == NULL_POINTER
+    lib.cufkb_block_backward_from_xyz.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    args = [16, 32, 48, None, None, None, 64, 80, 96, 112, 128]
+    assert lib.cufkb_block_backward_from_xyz(F32, *args[:6], None, *args[7:], 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_block_backward_from_xyz(BF16, *args[:6], None, *args[7:], 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_block_backward_from_xyz(F32, *args[:6], 66, *args[7:], 2, 10, None) == MISALIGNED
+    assert lib.cufkb_block_backward_from_xyz(F64, *args, 2, 2052, None) == TOO_MANY_STEPS
+    assert lib.cufkb_block_backward_from_xyz(F32, *args, 2, 3, None) == POINT_COUNT
+    assert lib.cufkb_block_backward_from_xyz(F32, *args, 0, 10, None) == SUCCESS
+    assert lib.cufkb_block_backward_from_xyz(7, *args, 2, 10, None) == INVALID_DTYPE
 
 
 def test_torsion_validation(lib):
