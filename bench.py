@@ -70,6 +70,7 @@ class Dist:
         if self.world != gpus and self.world > 1:
             raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
         self.pg = None
+        self.device = torch.device("cuda") if device_needed else torch.device("cpu")
         if self.world > 1:
             import datetime
 
@@ -94,7 +95,7 @@ class Dist:
     def max(self, value: float) -> float:
         if self.pg is None:
             return value
-        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 

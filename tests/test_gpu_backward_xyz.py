@@ -132,3 +132,21 @@ def test_chain_far_from_origin(offset):
     for got, rec, want in zip(from_xyz, recomputed, ref[1:]):
         assert _rel(got, want) <= 1e-4
         assert _rel(rec, want) <= 1e-4
+
+
+def test_full_size_linearity_and_agreement():
+    # config 1 size: the backward is linear in grad_xyz, and the xyz form agrees with the recompute
+    # form on every chain
+    inp = nerf64.make_inputs(4096, 768, seed=0)
+    L, A, D, G = (inp[k].cuda() for k in ("lengths", "angles", "dihedrals", "grad"))
+    G2 = torch.randn(G.shape, generator=torch.Generator().manual_seed(1)).cuda()
+    xyz = C.block_forward(L, A, D, None, None, None)
+    g1 = C.block_backward_from_xyz(L, A, D, None, None, None, xyz, G)
+    g2 = C.block_backward_from_xyz(L, A, D, None, None, None, xyz, G2)
+    g12 = C.block_backward_from_xyz(L, A, D, None, None, None, xyz, 2.0 * G - 3.0 * G2)
+    for a, b, c in zip(g1, g2, g12):
+        assert _rel(c, 2.0 * a - 3.0 * b) <= 1e-5
+    rec = C.block_backward(L, A, D, None, None, None, G)
+    for a, b in zip(g1, rec):
+        per_chain = ((a - b).double().norm(dim=1) / b.double().norm(dim=1)).max()
+        assert float(per_chain) <= 1e-4

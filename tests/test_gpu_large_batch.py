@@ -64,3 +64,17 @@ def test_chain_result_does_not_depend_on_the_batch():
     for r in (0, 1, 1199, 2399):
         one = cufk.reconstruct(L[r], A[r], D[r])
         assert float((big[r] - one).abs().max()) <= 1e-5
+
+
+def test_grid_beyond_65535_chains():
+    # one CTA per chain: 70000 chains need a grid larger than the 16-bit y/z grid limits
+    inp = nerf64.make_inputs(70000, 6, seed=8)
+    L, A, D = (inp[k].cuda().requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    xyz = cufk.reconstruct(L, A, D)
+    xyz.backward(inp["grad"].cuda())
+    rows = [0, 1, 35000, 65535, 65536, 69999]
+    c = {k: v[rows].double() for k, v in inp.items()}
+    ref = nerf64.reconstruct64_with_grads(c["lengths"], c["angles"], c["dihedrals"], c["grad"])
+    assert float((xyz.detach()[rows].double().cpu() - ref[0]).abs().max()) <= 1e-5
+    for got, want in zip((L.grad, A.grad, D.grad), ref[1:]):
+        assert float((got[rows].double().cpu() - want).norm() / want.norm()) <= 1e-5
