@@ -62,7 +62,6 @@ struct CtaExchange {
   V warp_sums[kMaxWarps * 6];  // suffix scan of (force, moment)
   V warp_red[kMaxWarps];       // first-frame reduction (separate: warps may still read warp_sums)
   V frame[12];                 // base frame F (row-major) and p2, built once by thread 0
-  int general;                 // backward: base frame not orthonormal (set by thread 0)
 };
 
 // The chain's first frame from its anchors and (lengths[0], lengths[1], angles[0]), read from
@@ -235,7 +234,7 @@ template <typename T, typename V, typename StepFn>
 __device__ __forceinline__ Affine<V> sweep_local_prefix(const ChainViews<T>& cv, StepRange r, StepFn step) {
   Affine<V> P = affine_identity<V>();
   int off = 3 * (r.first + 3);
-#pragma unroll 4
+#pragma unroll 2  // 2, not 4: the inlined sine/cosine makes a 4-step body large enough to cost time
   for (int k = 0; k < r.count; ++k, off += 3) {
     advance(P, step(r.first + k));
     cv.set_slot(off, P.v[0]);
@@ -640,12 +639,15 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     const R a0 = to_r<R>(args.angles[chain * (N - 2)]);
     return FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
   };
-  if (tid == 0) ex.general = first_frame().bf.general ? 1 : 0;
+  // thread 0 builds the first frame while the rows stage and keeps it in shared memory for the
+  // first-frame gradients at the end (no dependent global loads on the CTA's critical path there)
+  __shared__ FirstFrame<V> first;
+  if (tid == 0) first = first_frame();
   const StepRange range = step_range(tid, K, St);
   cp_async_wait_all();
   __syncthreads();
 
-  const bool general = ex.general != 0;  // uniform over the CTA
+  const bool general = first.bf.general;  // uniform over the CTA
   bool redo = general;
   if (!redo) {
     // moments about o = p2 (the chain's own origin, atom 2 of the forward's xyz): tau then loses no
@@ -730,15 +732,12 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     // non-finite value: the comparisons fail) send the chain to the recompute form.
     const bool bad = range.count > 0 && !(dmin2 >= static_cast<V>(1e-6) * xmax2 && wmin2 >= static_cast<V>(1e-2));
     redo = __syncthreads_or(bad) != 0;
-    if (!redo && tid == 0) {
-      const FirstFrame<V> f = first_frame();
-      first_frame_grads<true, T, V, true>(cv, f.af, f.bf, grow, F3, M3, V(0));
-    }
+    // g1, g2 from the staged grad row: slots 1 and 2 are not overwritten by the sweep
+    if (!redo && tid == 0) first_frame_grads<true, T, V, true>(cv, first.af, first.bf, cv.G, F3, M3, V(0));
   }
   if (redo) {
-    const FirstFrame<V> f = first_frame();
-    const AnchorFrame<V>& af = f.af;
-    const BackwardFrame<V>& bf = f.bf;
+    const AnchorFrame<V>& af = first.af;
+    const BackwardFrame<V>& bf = first.bf;
     // recompute form, laid out as in block_backward_kernel: inputs into the slots, grad row restaged
     __syncthreads();
     stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
