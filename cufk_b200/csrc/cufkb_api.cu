@@ -23,10 +23,18 @@ constexpr int kMaxDevices = 64;
 constexpr int kNumKernels = 20;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
+// Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
+// fixed work (staging, suffix scan, first frame) is large next to its per-step work, so fewer,
+// longer threads per chain beat more resident warps (measured on B200: at N=768, 2 warps per chain
+// and ~22 resident warps beat 3 warps per chain and 24).
 #ifndef CUFKB_TARGET_WARPS_PER_SM
 #define CUFKB_TARGET_WARPS_PER_SM 32
 #endif
-constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;  // resident warps per SM the plan aims for
+#ifndef CUFKB_XYZ_TARGET_WARPS_PER_SM
+#define CUFKB_XYZ_TARGET_WARPS_PER_SM 20
+#endif
+constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;
+constexpr int kXyzTargetWarpsPerSm = CUFKB_XYZ_TARGET_WARPS_PER_SM;
 
 struct DeviceCache {
   std::once_flag once;
@@ -142,17 +150,17 @@ int resident_warps(const DeviceCache& d, const KernelCache& k, size_t dyn_smem, 
   return chains * warps;
 }
 
-Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCache& k, size_t dyn_smem) {
+Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCache& k, size_t dyn_smem, int target) {
   const int steps = points - 3;
   int warps = ceil_div(steps, cufkb::kWarp * kTargetItems);
   if (warps < 1) warps = 1;
   if (warps > cufkb::kMaxWarps) warps = cufkb::kMaxWarps;
   auto splittable = [&](int w) { return w < cufkb::kMaxWarps && ceil_div(steps, cufkb::kWarp * (w + 1)) >= kMinItems; };
-  while (splittable(warps) && resident_warps(d, k, dyn_smem, warps) < kTargetWarpsPerSm &&
+  while (splittable(warps) && resident_warps(d, k, dyn_smem, warps) < target &&
          resident_warps(d, k, dyn_smem, warps + 1) > resident_warps(d, k, dyn_smem, warps)) {
     ++warps;
   }
-  const int64_t grid_target = int64_t(d.sm_count) * kTargetWarpsPerSm;
+  const int64_t grid_target = int64_t(d.sm_count) * target;
   while (splittable(warps) && batch * warps < grid_target) ++warps;
   int items = ceil_div(steps, cufkb::kWarp * warps);
   if ((items & 1) == 0) ++items;
@@ -192,7 +200,7 @@ struct LaunchEnv {
 
 // Device, kernel footprint, shared-memory opt-in and plan of one launch.
 template <typename Kernel>
-int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem) {
+int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem, int target = kTargetWarpsPerSm) {
   const int e = current_device(&env->dev);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   env->cache = device_cache(env->dev);
@@ -201,7 +209,7 @@ int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int 
   if (k->error != 0) return fail_cuda(static_cast<cudaError_t>(k->error));
   if (static_cast<int>(smem) + k->static_smem > env->cache->max_smem_optin) return fail_cuda(cudaErrorInvalidValue);
   if (cudaError_t err = ensure_smem_limit(kernel, &g_kernels[kernel_id], env->dev, env->cache->max_smem_optin)) return fail_cuda(err);
-  env->plan = make_plan(batch, points, *env->cache, *k, smem);
+  env->plan = make_plan(batch, points, *env->cache, *k, smem, target);
   return CUFKB_SUCCESS;
 }
 
@@ -255,7 +263,7 @@ int block_backward_xyz_impl(const void* L, const void* A, const void* D, const v
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_xyz_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardXyz, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardXyz, dtype_index<T>()), batch, points, smem, kXyzTargetWarpsPerSm)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
