@@ -20,7 +20,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 20;
+constexpr int kNumKernels = 24;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -221,8 +221,8 @@ constexpr int dtype_index() {
   return 3;
 }
 
-// Kernel ids for the caches: kind (5) x dtype (4).
-enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardXyz = 4 };
+// Kernel ids for the caches: kind (6) x dtype (4).
+enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardXyz = 4, kTorsionBackwardXyz = 5 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 template <typename T>
@@ -309,6 +309,23 @@ int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsi
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                           static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Torsion backward from the forward's xyz (32- and 64-bit types).
+template <typename T>
+int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* xyz, const void* g, void* graw,
+                              int64_t grad_stride, int64_t batch, int points, cudaStream_t stream) {
+  using R = typename cufkb::ComputeOf<T>::type;
+  const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
+  auto kernel = cufkb::torsion_backward_xyz_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackwardXyz, dtype_index<T>()), batch, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                          static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(graw),
+                                                                          grad_stride, geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
@@ -458,6 +475,29 @@ int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_str
       return torsion_backward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch,
                                                   n, s);
   }
+}
+
+int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                                    const void* xyz, const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch,
+                                    int64_t points, cufkb_stream_t stream) {
+  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
+    if (int st = check_shape(dtype, batch, points)) return st;
+    if (batch > 0 && !xyz) return CUFKB_ERROR_NULL_POINTER;
+    return cufkb_torsion_backward(dtype, raw_pairs, raw_row_stride, constants, grad_xyz, grad_raw_pairs, grad_row_stride, batch, points, stream);
+  }
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!raw_pairs || !xyz || !grad_xyz || !grad_raw_pairs) return CUFKB_ERROR_NULL_POINTER;
+  if (!constants) return CUFKB_ERROR_INVALID_VALUE;
+  if (raw_row_stride < 0 || grad_row_stride < 0 || (batch > 1 && grad_row_stride < 2 * (points - 3))) return CUFKB_ERROR_BAD_STRIDE;
+  const size_t es = elem_size(dtype);
+  if (!aligned(raw_pairs, es) || !aligned(xyz, es) || !aligned(grad_xyz, es) || !aligned(grad_raw_pairs, es)) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    return torsion_backward_xyz_impl<float>(raw_pairs, raw_row_stride, constants, xyz, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
+  }
+  return torsion_backward_xyz_impl<double>(raw_pairs, raw_row_stride, constants, xyz, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
 }
 
 const char* cufkb_status_string(int status) {

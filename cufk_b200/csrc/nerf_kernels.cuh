@@ -5,6 +5,7 @@
 // block_backward_xyz_kernel        the same gradients from the forward's xyz (no local transforms)
 // torsion_forward_kernel        <- src/cufk/csrc/torsion.cu:254-295 (xyz from raw (sin, cos) pairs)
 // torsion_backward_kernel       <- src/cufk/csrc/torsion.cu:297-381 (d raw pairs)
+// torsion_backward_xyz_kernel      the same from the forward's xyz (as the reference's own does)
 //
 // One CTA reconstructs one chain with W = blockDim.x / 32 warps and K (odd) consecutive steps per
 // thread.
@@ -869,36 +870,13 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kMaxWarps* kWarp)
-    torsion_backward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
-                            const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride, ChainGeometry geo) {
-  using R = typename ComputeOf<T>::type;
-  using V = R;
-  constexpr bool kScatter = sizeof(T) >= 4;
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ CtaExchange<V> ex;
-
-  const int N = geo.points, St = geo.steps, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const int64_t chain = blockIdx.x;
-  const T* raw = raw_pairs + chain * raw_stride;
-  ChainViews<T> cv;
-  unsigned char* p = smem;
-  cv.X = reinterpret_cast<R*>(p);
-  p += slot_bytes(N, sizeof(R));
-  if constexpr (kScatter) {
-    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
-  } else {
-    cv.row[0] = stage_row_async(p, raw, 2 * St, tid, nthr);
-    p += staged_row_bytes(size_t(2) * St, sizeof(T));
-  }
-  cv.G = stage_row_async(p, grad_xyz + chain * 3 * N, 3 * N, tid, nthr);
+// Recompute form of the torsion backward after staging (raw pairs in the slots or a staged row,
+// grad row in cv.G): the same structure as the block recompute form; d raw goes into the slots.
+template <typename T, typename V, typename R>
+__device__ __forceinline__ void torsion_backward_recompute(const ChainViews<T>& cv, CtaExchange<V>& ex, const TorsionConsts<R>& consts, StepRange range,
+                                                           int nwarps) {
   V F[9], p1[3], p2[3];
   torsion_base<V>(consts, F, p1, p2);
-  cp_async_wait_all();
-  __syncthreads();
-
   auto step = [&](int s) {
     V rs, rc;
     torsion_pair<T>(cv, s, rs, rc);
@@ -907,9 +885,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_constants_for(consts, s, l, st, ct);
     return step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv));
   };
-
   // the fixed torsion base frame is orthonormal: world coordinates throughout
-  const StepRange range = step_range(tid, K, St);
   V gsum[3];
   V Q[9];
   const Affine<V> total = sweep_backward_totals<true, T, V>(cv, F, range, step, gsum, Q);
@@ -946,15 +922,186 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
       Ms[i] = vsub(Ms[i], mx[i]);
     }
     // raw-pair chain rule (torsion.cu:173-182): d raw = d phi * (c, -s) / n2
-    const V scale = d_phi / n2;
+    const V scale = vmul(d_phi, vmul(rinv, rinv));
     cv.set_slot(off + 1, vmul(rc, scale));
     cv.set_slot(off + 2, vneg(vmul(rs, scale)));
   }
-  __syncthreads();
-  T* gr = grad_raw + chain * grad_stride;
-  const R* X = cv.X;
+}
+
+// d raw from the slots (written by the recompute form) to the output row.
+template <typename T, typename R>
+__device__ __forceinline__ void write_pair_grads(const R* X, T* gr, int S, int tid, int nthr) {
 #pragma unroll 4
-  for (int e = tid; e < 2 * St; e += nthr) gr[e] = from_r<T>(X[3 * ((e >> 1) + 3) + 1 + (e & 1)]);
+  for (int e = tid; e < 2 * S; e += nthr) gr[e] = from_r<T>(X[3 * ((e >> 1) + 3) + 1 + (e & 1)]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    torsion_backward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
+                            const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride, ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  constexpr bool kScatter = sizeof(T) >= 4;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const int64_t chain = blockIdx.x;
+  const T* raw = raw_pairs + chain * raw_stride;
+  ChainViews<T> cv;
+  unsigned char* p = smem;
+  cv.X = reinterpret_cast<R*>(p);
+  p += slot_bytes(N, sizeof(R));
+  if constexpr (kScatter) {
+    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
+  } else {
+    cv.row[0] = stage_row_async(p, raw, 2 * St, tid, nthr);
+    p += staged_row_bytes(size_t(2) * St, sizeof(T));
+  }
+  cv.G = stage_row_async(p, grad_xyz + chain * 3 * N, 3 * N, tid, nthr);
+  cp_async_wait_all();
+  __syncthreads();
+  torsion_backward_recompute<T, V, R>(cv, ex, consts, step_range(tid, K, St), nwarps);
+  __syncthreads();
+  write_pair_grads<T, R>(cv.X, grad_raw + chain * grad_stride, St, tid, nthr);
+}
+
+// Torsion backward from the forward's xyz (4- and 8-byte types), as the reference's own torsion
+// backward does (world_torsion_grad, torsion.cu:213-217 and :297-381): d phi_s = u_{s+1} . tau_s
+// with u_{s+1} the direction of bond (x_{s+1}, x_{s+2}) and tau_s = M_s - (x_{s+2} - o) x F_s, the
+// sums over atoms >= s+3 (moments about o = atom 2).  The xyz and grad rows are staged (16-byte
+// LDGSTS); d phi goes over the grad row; the last loop applies the raw-pair chain rule
+// d raw = d phi (c, -s) / n2 reading each raw element once from global memory, its partner (sin
+// or cos) from the neighbouring lane.  A bond shorter than 1e-3 |x|max, a pair below the norm
+// clamp (not a rotation), or a non-finite value sends the chain to the recompute form.
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    torsion_backward_xyz_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
+                                const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride,
+                                ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const int64_t chain = blockIdx.x;
+  const T* raw = raw_pairs + chain * raw_stride;
+  const T* grow = grad_xyz + chain * 3 * N;
+  unsigned char* const slot_region = smem;
+  unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
+  ChainViews<T> cv;
+  cv.Y = stage_row_async(slot_region, xyz + chain * 3 * N, 3 * N, tid, nthr);
+  cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
+  // the raw row is read once, by the chain-rule loop at the end: bring it into L2 meanwhile
+  for (int line = tid; line * 128 < 2 * St * int(sizeof(T)); line += nthr) prefetch_l2(reinterpret_cast<const char*>(raw) + line * 128);
+  const StepRange range = step_range(tid, K, St);
+  cp_async_wait_all();
+  __syncthreads();
+
+  const V o[3] = {cv.pos(6), cv.pos(7), cv.pos(8)};
+  V gsum[3] = {V(0), V(0), V(0)};
+  V msum[3] = {V(0), V(0), V(0)};
+  V xmax2 = V(0);
+  int off = 3 * (range.first + 3);
+#pragma unroll 2
+  for (int k = 0; k < range.count; ++k, off += 3) {
+    const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+    const V xw[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+    xmax2 = fmax(xmax2, dot3(xw, xw));
+    const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
+    V mx[3];
+    cross3(x, g, mx);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      gsum[i] = vadd(gsum[i], g[i]);
+      msum[i] = vadd(msum[i], mx[i]);
+    }
+  }
+  V Fs[3], Ms[3];
+  suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
+  // sweep: x1 = x_{s+1}, x2 = x_{s+2} carried (threads without steps read nothing)
+  V x1[3] = {V(0), V(0), V(0)};
+  V x2[3] = {V(0), V(0), V(0)};
+  if (range.count > 0) {
+    off = 3 * (range.first + 1);  // atoms first+1 and first+2 <= N-2
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      x1[i] = cv.pos(off + i);
+      x2[i] = cv.pos(off + 3 + i);
+    }
+  }
+  V dmin2 = V(1e30);
+  off = 3 * (range.first + 3);
+#pragma unroll 2
+  for (int k = 0; k < range.count; ++k, off += 3) {
+    const V x3[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
+    const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+    const V d[3] = {vsub(x2[0], x1[0]), vsub(x2[1], x1[1]), vsub(x2[2], x1[2])};
+    const V d2 = dot3(d, d);
+    dmin2 = fmin(dmin2, d2);
+    const V inv = vrsqrt(d2);
+    const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+    V xf[3];
+    cross3(xr, Fs, xf);
+    const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
+    const V d_phi = vmul(dot3(d, tau), inv);
+    const V x3r[3] = {vsub(x3[0], o[0]), vsub(x3[1], o[1]), vsub(x3[2], o[2])};
+    V mx[3];
+    cross3(x3r, g, mx);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      Fs[i] = vsub(Fs[i], g[i]);
+      Ms[i] = vsub(Ms[i], mx[i]);
+      x1[i] = x2[i];
+      x2[i] = x3[i];
+    }
+    cv.G[off] = d_phi;
+  }
+  // the last bond of the thread's range is x_{first+count+1} -> x_{first+count+2}: covered, every
+  // bond a step uses is tested; non-finite values fail the comparison
+  const bool bad = range.count > 0 && !(dmin2 >= static_cast<V>(1e-6) * xmax2);
+  bool redo = __syncthreads_or(bad) != 0;
+  T* gr = grad_raw + chain * grad_stride;
+  if (!redo) {
+    // chain rule, warp-uniform trip count so that every lane takes part in the shuffle.  A pair
+    // below the norm clamp is not normalised to a unit pair: that step is not a rotation, the
+    // positions cannot give its gradient, and the chain is redone below.
+    const int lane = tid & (kWarp - 1);
+    bool clamped = false;
+#pragma unroll 16  // the raw loads of 16 iterations in flight at once
+    for (int e0 = tid - lane; e0 < 2 * St; e0 += nthr) {
+      const int e = e0 + lane;
+      const bool live = e < 2 * St;
+      const V v = live ? to_r<V>(raw[e]) : V(1);
+      const V partner = shfl_xor(v, 1);
+      const V rs = (e & 1) ? partner : v;
+      const V rc = (e & 1) ? v : partner;
+      const V n2raw = vfma(rs, rs, vmul(rc, rc));
+      clamped |= !(n2raw >= static_cast<V>(1.0e-8f * 1.0e-8f));
+      const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+      if (live) {
+        const V scale = vmul(cv.G[3 * ((e >> 1) + 3)], vmul(rinv, rinv));
+        gr[e] = from_r<T>((e & 1) ? vneg(vmul(rs, scale)) : vmul(rc, scale));
+      }
+    }
+    redo = __syncthreads_or(clamped) != 0;
+  }
+  if (redo) {
+    // recompute form, laid out as in torsion_backward_kernel
+    __syncthreads();
+    cv.X = reinterpret_cast<R*>(slot_region);
+    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
+    cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
+    cp_async_wait_all();
+    __syncthreads();
+    torsion_backward_recompute<T, V, R>(cv, ex, consts, range, nwarps);
+    __syncthreads();
+    write_pair_grads<T, R>(cv.X, gr, St, tid, nthr);
+  }
 }
 
 }  // namespace cufkb

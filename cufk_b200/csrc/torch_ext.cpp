@@ -246,26 +246,41 @@ Tensor torsion_forward_impl(const Tensor& raw, const std::vector<double>& consts
   return xyz;
 }
 
+// gradient tensor with raw's strides (empty_strided_like, extension_utils.cuh:162-164); rows that
+// would overlap (a broadcast row stride) get a contiguous gradient instead
+Tensor pair_grad_like(const Tensor& raw, const Shape& shape) {
+  return (shape.batch <= 1 || raw.stride(0) >= raw.size(1)) ? torch::empty_strided(raw.sizes(), raw.strides(), raw.options())
+                                                            : torch::empty(raw.sizes(), raw.options());
+}
+
+Tensor torsion_backward_xyz_impl(const Tensor& raw, const std::vector<double>& consts, const Tensor& xyz, const Tensor& grad_points, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(raw.device());
+  const cufkb_torsion_constants c = torsion_constants(consts);
+  Tensor grad = pair_grad_like(raw, shape);
+  check_status(cufkb_torsion_backward_from_xyz(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr(),
+                                               grad_points.data_ptr(), grad.data_ptr(), grad.stride(0), shape.batch, shape.points,
+                                               current_stream()),
+               "torsion_pairs backward");
+  return grad;
+}
+
 Tensor torsion_backward_impl(const Tensor& raw, const std::vector<double>& consts, const Tensor& grad_points, const Shape& shape) {
   const c10::cuda::CUDAGuard guard(raw.device());
   const cufkb_torsion_constants c = torsion_constants(consts);
-  // the reference copies raw's strides (empty_strided_like, extension_utils.cuh:162-164); rows that
-  // would overlap (a broadcast row stride) get a contiguous gradient instead
-  Tensor grad = (shape.batch <= 1 || raw.stride(0) >= raw.size(1)) ? torch::empty_strided(raw.sizes(), raw.strides(), raw.options())
-                                                                    : torch::empty(raw.sizes(), raw.options());
+  Tensor grad = pair_grad_like(raw, shape);
   check_status(cufkb_torsion_backward(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, grad_points.data_ptr(),
                                       grad.data_ptr(), grad.stride(0), shape.batch, shape.points, current_stream()),
                "torsion_pairs backward");
   return grad;
 }
 
-// torsion.cu:419-437; the forward saves only raw_pairs (the backward recomputes the chain)
+// torsion.cu:419-437: the forward saves raw_pairs and its output, which the backward reads
 class TorsionAutograd : public torch::autograd::Function<TorsionAutograd> {
  public:
   static Tensor forward(AutogradContext* ctx, Tensor raw_pairs, std::vector<double> consts) {
     const Shape shape = check_pairs(raw_pairs);
     Tensor xyz = torsion_forward_impl(raw_pairs, consts, shape);
-    ctx->save_for_backward({raw_pairs});
+    ctx->save_for_backward({raw_pairs, xyz});
     ctx->saved_data["consts"] = c10::IValue(consts);
     return xyz;
   }
@@ -277,7 +292,7 @@ class TorsionAutograd : public torch::autograd::Function<TorsionAutograd> {
     Tensor grad_points = grad_outputs[0].is_contiguous() ? grad_outputs[0] : grad_outputs[0].contiguous();
     check_like(grad_points, raw, "grad_points");
     const Shape shape = check_pairs(raw);
-    return {torsion_backward_impl(raw, consts, grad_points, shape), Tensor()};
+    return {torsion_backward_xyz_impl(raw, consts, saved[1], grad_points, shape), Tensor()};
   }
 };
 
@@ -323,6 +338,15 @@ Tensor torsion_backward(const Tensor& raw, const std::vector<double>& consts, co
   return torsion_backward_impl(raw, consts, grad_points, shape);
 }
 
+Tensor torsion_backward_from_xyz(const Tensor& raw, const std::vector<double>& consts, const Tensor& xyz, const Tensor& grad_points) {
+  const Shape shape = check_pairs(raw);
+  check_like(grad_points, raw, "grad_points");
+  check_like(xyz, raw, "xyz");
+  TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
+  TORCH_CHECK(xyz.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}) && xyz.is_contiguous(), "xyz must be the (B, N, 3) output of the forward");
+  return torsion_backward_xyz_impl(raw, consts, xyz, grad_points, shape);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -341,5 +365,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("xyz"), pybind11::arg("grad_points"));
   m.def("torsion_forward", &torsion_forward, "torsion forward kernel only");
   m.def("torsion_backward", &torsion_backward, "torsion backward kernel only");
+  m.def("torsion_backward_from_xyz", &torsion_backward_from_xyz, "torsion backward kernel reading the forward's xyz");
   m.def("max_point_count", &cufkb_max_point_count);
 }

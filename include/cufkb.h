@@ -22,6 +22,7 @@
  *   cufkb_block_backward_from_xyz <- backward_cuda_impl<T> as well (same gradients, reads xyz)
  *   cufkb_torsion_forward <- forward_default_impl<T> src/cufk/csrc/torsion.cu:387-397
  *   cufkb_torsion_backward<- backward_xyz_impl<T>   src/cufk/csrc/torsion.cu:399-411
+ *   cufkb_torsion_backward_from_xyz <- backward_xyz_impl<T> as well (reads the saved xyz, like it)
  *   validation codes      <- TORCH_CHECKs of src/cufk/csrc/extension_utils.cuh:57-143
  */
 #ifndef CUFKB_H_
@@ -113,6 +114,16 @@ CUFKB_API int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t ra
 CUFKB_API int cufkb_torsion_backward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
                            const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
                            cufkb_stream_t stream);
+
+/* The same gradient as cufkb_torsion_backward, from xyz = the output of cufkb_torsion_forward with
+ * identical arguments, as the reference's own torsion backward reads its saved xyz
+ * (src/cufk/csrc/torsion.cu:297-381): d dihedral = bond direction . torque, no chain rebuilt.
+ * Chains with a bond shorter than 1e-3 of the largest coordinate are recomputed in the same
+ * kernel.  float16/bfloat16 ignore xyz and recompute.  Replaces backward_xyz_impl<T>. */
+CUFKB_API int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, int64_t raw_row_stride,
+                                    const cufkb_torsion_constants* constants, const void* xyz, const void* grad_xyz,
+                                    void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
+                                    cufkb_stream_t stream);
 
 /* Static text for a status code. */
 CUFKB_API const char* cufkb_status_string(int status);

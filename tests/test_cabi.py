@@ -112,6 +112,19 @@ def test_torsion_validation(lib):
     assert lib.cufkb_torsion_backward(F32, 16, 14, ctypes.byref(c), 64, 128, 14, 0, 10, None) == SUCCESS
 
 
+def test_torsion_from_xyz_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_torsion_backward_from_xyz.argtypes = [ctypes.c_int, vp, i64, vp, vp, vp, vp, i64, i64, i64, vp]
+    c = TorsionConstants()
+    assert lib.cufkb_torsion_backward_from_xyz(F32, 16, 14, ctypes.byref(c), None, 64, 128, 14, 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_torsion_backward_from_xyz(BF16, 16, 14, ctypes.byref(c), None, 64, 128, 14, 2, 10, None) == NULL_POINTER
+    assert lib.cufkb_torsion_backward_from_xyz(F32, 16, 14, None, 32, 64, 128, 14, 2, 10, None) == INVALID_VALUE
+    assert lib.cufkb_torsion_backward_from_xyz(F32, 16, 14, ctypes.byref(c), 34, 64, 128, 14, 2, 10, None) == MISALIGNED
+    assert lib.cufkb_torsion_backward_from_xyz(F32, 16, 14, ctypes.byref(c), 32, 64, 128, 13, 2, 10, None) == BAD_STRIDE
+    assert lib.cufkb_torsion_backward_from_xyz(F32, 16, 14, ctypes.byref(c), 32, 64, 128, 14, 0, 10, None) == SUCCESS
+    assert lib.cufkb_torsion_backward_from_xyz(F64, 16, 14, ctypes.byref(c), 32, 64, 128, 14, 2, 2052, None) == TOO_MANY_STEPS
+
+
 def test_status_strings(lib):
     assert lib.cufkb_status_string(SUCCESS) == b"success"
     assert lib.cufkb_status_string(POINT_COUNT) == b"point_count must be >= 4"
