@@ -1,10 +1,12 @@
 """cufk_b200: B200-native (sm_100a) drop-in for cufk's reconstruction path.
 
 ``import cufk_b200 as cufk`` gives the reference's public surface (src/cufk/__init__.py:1-11):
-``reconstruct``, ``compile_torsion``, ``BLOCK_SCAN_MAX_POINT_COUNT`` and ``__version__``.
+``reconstruct``, ``compile_torsion``, ``BLOCK_SCAN_MAX_POINT_COUNT`` and ``__version__``; and
+``reconstruct_long`` for chains longer than ``BLOCK_SCAN_MAX_POINT_COUNT``, which the reference
+does not support.
 """
 
-from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct
+from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct, reconstruct_long
 from .torsion import compile_torsion
 
 __version__ = "0.1.0"
@@ -14,4 +16,5 @@ __all__ = [
     "__version__",
     "compile_torsion",
     "reconstruct",
+    "reconstruct_long",
 ]

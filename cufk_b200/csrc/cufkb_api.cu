@@ -7,6 +7,7 @@
 // register plan, block.cu:76-86), and anchors may be NULL for the defaults.
 #include "cufkb.h"
 #include "nerf_kernels.cuh"
+#include "nerf_long.cuh"
 
 #include <atomic>
 #include <cstdint>
@@ -20,7 +21,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 24;
+constexpr int kNumKernels = 40;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -221,8 +222,19 @@ constexpr int dtype_index() {
   return 3;
 }
 
-// Kernel ids for the caches: kind (6) x dtype (4).
-enum KernelKind { kBlockForward = 0, kBlockBackward = 1, kTorsionForward = 2, kTorsionBackward = 3, kBlockBackwardXyz = 4, kTorsionBackwardXyz = 5 };
+// Kernel ids for the caches: kind (10) x dtype (4).
+enum KernelKind {
+  kBlockForward = 0,
+  kBlockBackward = 1,
+  kTorsionForward = 2,
+  kTorsionBackward = 3,
+  kBlockBackwardXyz = 4,
+  kTorsionBackwardXyz = 5,
+  kLongTotals = 6,
+  kLongForward = 7,
+  kLongSums = 8,
+  kLongBackward = 9
+};
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 template <typename T>
@@ -327,6 +339,90 @@ int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_t
                                                                           static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(graw),
                                                                           grad_stride, geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// ---- chains longer than one CTA: segments of at most CUFKB_MAX_STEPS steps ----
+struct LongPlan {
+  int segs;
+  int seg_steps;
+};
+
+LongPlan long_plan(int64_t points) {
+  const int64_t steps = points - 3;
+  const int64_t segs = (steps + CUFKB_MAX_STEPS - 1) / CUFKB_MAX_STEPS;
+  return {static_cast<int>(segs), static_cast<int>((steps + segs - 1) / segs)};
+}
+
+// workspace words: the totals (12 per segment) then the sums (6 per segment)
+size_t long_workspace_words(int64_t batch, const LongPlan& lp) {
+  return static_cast<size_t>(batch) * lp.segs * (cufkb::kTotalWords + cufkb::kSumWords);
+}
+
+template <typename T>
+int long_totals_launch(const cufkb::BlockArgs<T>& args, typename cufkb::ComputeOf<T>::type* totals, int64_t batch, int64_t points, const LongPlan& lp,
+                       cudaStream_t stream) {
+  const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, false);
+  auto kernel = cufkb::long_totals_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kLongTotals, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
+  const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int block_forward_long_impl(const cufkb::BlockArgs<T>& args, void* xyz, int64_t batch, int64_t points, void* workspace, cudaStream_t stream) {
+  using R = typename cufkb::ComputeOf<T>::type;
+  const LongPlan lp = long_plan(points);
+  R* totals = static_cast<R*>(workspace);
+  if (int st = long_totals_launch<T>(args, totals, batch, points, lp, stream)) return st;
+  const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, false);
+  auto kernel = cufkb::long_forward_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kLongForward, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
+  const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, static_cast<T*>(xyz), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+int block_backward_long_impl(const cufkb::BlockArgs<T>& args, const void* xyz, const void* g, void* gL, void* gA, void* gD, int64_t batch,
+                             int64_t points, void* workspace, cudaStream_t stream) {
+  using R = typename cufkb::ComputeOf<T>::type;
+  const LongPlan lp = long_plan(points);
+  R* totals = static_cast<R*>(workspace);
+  R* sums = totals + static_cast<size_t>(batch) * lp.segs * cufkb::kTotalWords;
+  if (int st = long_totals_launch<T>(args, totals, batch, points, lp, stream)) return st;
+  {
+    auto kernel = cufkb::long_sums_kernel<T>;
+    LaunchEnv env;
+    if (int st = launch_env(&env, kernel, kernel_id(kLongSums, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, 0)) return st;
+    const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
+    kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, 0, stream>>>(static_cast<const T*>(xyz), static_cast<const T*>(g), sums, geo);
+    if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  }
+  const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, true);
+  auto kernel = cufkb::long_backward_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kLongBackward, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
+  const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, sums, static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                                    static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Validation shared by the long entry points (dtype float32/float64, 4 <= N <= INT32_MAX,
+// B * segments within one grid).
+int check_long(int dtype, int64_t batch, int64_t points) {
+  if (elem_size(dtype) == 0) return CUFKB_ERROR_INVALID_DTYPE;
+  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || batch > INT32_MAX || points > INT32_MAX) return CUFKB_ERROR_SHAPE_LIMITS;
+  if (points < 4) return CUFKB_ERROR_POINT_COUNT;
+  if (batch * long_plan(points).segs > INT32_MAX) return CUFKB_ERROR_SHAPE_LIMITS;
   return CUFKB_SUCCESS;
 }
 
@@ -500,6 +596,60 @@ int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, int64_t ra
   return torsion_backward_xyz_impl<double>(raw_pairs, raw_row_stride, constants, xyz, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
 }
 
+int cufkb_block_long_workspace_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes) {
+  if (!bytes) return CUFKB_ERROR_NULL_POINTER;
+  *bytes = 0;
+  if (int st = check_long(dtype, batch, points)) return st;
+  *bytes = long_workspace_words(batch, long_plan(points)) * elem_size(dtype);
+  return CUFKB_SUCCESS;
+}
+
+int cufkb_block_forward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                             const void* initial_normal, void* xyz, int64_t batch, int64_t points, void* workspace, size_t workspace_bytes,
+                             cufkb_stream_t stream) {
+  if (int st = check_long(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, workspace}, {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz})) {
+    return st;
+  }
+  if (!aligned(workspace, 16)) return CUFKB_ERROR_MISALIGNED;
+  const LongPlan lp = long_plan(points);
+  if (workspace_bytes < static_cast<size_t>(batch) * lp.segs * cufkb::kTotalWords * elem_size(dtype)) return CUFKB_ERROR_WORKSPACE;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    const cufkb::BlockArgs<float> a{static_cast<const float*>(lengths), static_cast<const float*>(angles), static_cast<const float*>(dihedrals),
+                                    static_cast<const float*>(p0), static_cast<const float*>(first_direction), static_cast<const float*>(initial_normal)};
+    return block_forward_long_impl<float>(a, xyz, batch, points, workspace, s);
+  }
+  const cufkb::BlockArgs<double> a{static_cast<const double*>(lengths), static_cast<const double*>(angles), static_cast<const double*>(dihedrals),
+                                   static_cast<const double*>(p0), static_cast<const double*>(first_direction), static_cast<const double*>(initial_normal)};
+  return block_forward_long_impl<double>(a, xyz, batch, points, workspace, s);
+}
+
+int cufkb_block_backward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                              const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
+                              void* grad_dihedrals, int64_t batch, int64_t points, void* workspace, size_t workspace_bytes, cufkb_stream_t stream) {
+  if (int st = check_long(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals, workspace},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
+  }
+  if (!aligned(workspace, 16)) return CUFKB_ERROR_MISALIGNED;
+  const LongPlan lp = long_plan(points);
+  if (workspace_bytes < long_workspace_words(batch, lp) * elem_size(dtype)) return CUFKB_ERROR_WORKSPACE;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    const cufkb::BlockArgs<float> a{static_cast<const float*>(lengths), static_cast<const float*>(angles), static_cast<const float*>(dihedrals),
+                                    static_cast<const float*>(p0), static_cast<const float*>(first_direction), static_cast<const float*>(initial_normal)};
+    return block_backward_long_impl<float>(a, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals, batch, points, workspace, s);
+  }
+  const cufkb::BlockArgs<double> a{static_cast<const double*>(lengths), static_cast<const double*>(angles), static_cast<const double*>(dihedrals),
+                                   static_cast<const double*>(p0), static_cast<const double*>(first_direction), static_cast<const double*>(initial_normal)};
+  return block_backward_long_impl<double>(a, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals, batch, points, workspace, s);
+}
+
 const char* cufkb_status_string(int status) {
   switch (status) {
     case CUFKB_SUCCESS:
@@ -522,6 +672,10 @@ const char* cufkb_status_string(int status) {
       return "torsion constants must not be NULL";
     case CUFKB_ERROR_CUDA:
       return "CUDA runtime error";
+    case CUFKB_ERROR_WORKSPACE:
+      return "workspace is smaller than cufkb_block_long_workspace_bytes";
+    case CUFKB_ERROR_UNSUPPORTED_DTYPE:
+      return "chains longer than 2051 points support float32 and float64";
     default:
       return "unknown status";
   }

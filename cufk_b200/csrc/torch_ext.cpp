@@ -133,9 +133,9 @@ struct Anchors {
   Tensor p0, first_direction, initial_normal;
 };
 
-Anchors checked_anchors(const Tensor& p0, const Tensor& fd, const Tensor& nn, const Tensor& ref, const Shape& shape) {
+Anchors checked_anchors(const Tensor& p0, const Tensor& fd, const Tensor& nn, const Tensor& ref, const Shape& shape, bool step_cap = true) {
   Anchors a{checked_anchor(p0, ref, "p0"), checked_anchor(fd, ref, "first_direction"), checked_anchor(nn, ref, "initial_normal")};
-  check_max_local_transforms(shape, "reconstruct");
+  if (step_cap) check_max_local_transforms(shape, "reconstruct");
   return a;
 }
 
@@ -216,6 +216,73 @@ class ReconstructAutograd : public torch::autograd::Function<ReconstructAutograd
     return {grads[0], grads[1], grads[2], Tensor(), Tensor(), Tensor()};
   }
 };
+
+// ---- chains of any length (segments of at most 2048 steps; no counterpart in the reference) ----
+Tensor long_workspace(const Tensor& like, const Shape& shape) {
+  size_t bytes = 0;
+  check_status(cufkb_block_long_workspace_bytes(dtype_code(like.scalar_type()), shape.batch, shape.points, &bytes), "reconstruct_long");
+  return torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
+}
+
+Tensor block_forward_long_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor xyz = torch::empty({shape.batch, shape.points, 3}, lengths.options());
+  Tensor ws = long_workspace(lengths, shape);
+  check_status(cufkb_block_forward_long(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                        ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
+                                        shape.batch, shape.points, ws.data_ptr(), static_cast<size_t>(ws.numel()), current_stream()),
+               "reconstruct_long");
+  return xyz;
+}
+
+std::vector<Tensor> block_backward_long_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Tensor& xyz,
+                                             const Tensor& grad_points, const Shape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor gl = torch::empty_like(lengths);
+  Tensor ga = torch::empty_like(angles);
+  Tensor gd = torch::empty_like(dihedrals);
+  Tensor ws = long_workspace(lengths, shape);
+  check_status(cufkb_block_backward_long(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                         ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
+                                         grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(), shape.batch, shape.points,
+                                         ws.data_ptr(), static_cast<size_t>(ws.numel()), current_stream()),
+               "reconstruct_long backward");
+  return {gl, ga, gd};
+}
+
+class LongAutograd : public torch::autograd::Function<LongAutograd> {
+ public:
+  static Tensor forward(AutogradContext* ctx, Tensor lengths, Tensor angles, Tensor dihedrals, std::optional<Tensor> p0,
+                        std::optional<Tensor> first_direction, std::optional<Tensor> initial_normal) {
+    const Shape shape = check_geom(lengths, angles, dihedrals);
+    const Anchors a = checked_anchors(opt(p0), opt(first_direction), opt(initial_normal), lengths, shape, /*step_cap=*/false);
+    Tensor xyz = block_forward_long_impl(lengths, angles, dihedrals, a, shape);
+    ctx->save_for_backward({lengths, angles, dihedrals, xyz});
+    ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
+    ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
+    ctx->saved_data["initial_normal"] = a.initial_normal.defined() ? c10::IValue(a.initial_normal) : c10::IValue();
+    return xyz;
+  }
+
+  static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+    const auto saved = ctx->get_saved_variables();
+    Tensor grad_points = grad_outputs[0].is_contiguous() ? grad_outputs[0] : grad_outputs[0].contiguous();
+    check_like(grad_points, saved[0], "grad_points");
+    const Shape shape = check_geom(saved[0], saved[1], saved[2]);
+    auto anchor = [&](const char* key) {
+      const c10::IValue& v = ctx->saved_data[key];
+      return v.isTensor() ? v.toTensor() : Tensor();
+    };
+    const Anchors a{anchor("p0"), anchor("first_direction"), anchor("initial_normal")};
+    auto grads = block_backward_long_impl(saved[0], saved[1], saved[2], a, saved[3], grad_points, shape);
+    return {grads[0], grads[1], grads[2], Tensor(), Tensor(), Tensor()};
+  }
+};
+
+Tensor apply_long(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                  const std::optional<Tensor>& first_direction, const std::optional<Tensor>& initial_normal) {
+  return LongAutograd::apply(lengths, angles, dihedrals, p0, first_direction, initial_normal);
+}
 
 Tensor apply_autograd(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
                       const std::optional<Tensor>& first_direction, const std::optional<Tensor>& initial_normal) {
@@ -351,6 +418,9 @@ Tensor torsion_backward_from_xyz(const Tensor& raw, const std::vector<double>& c
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("apply", &apply_autograd, "reconstruct autograd apply", pybind11::arg("lengths"), pybind11::arg("angles"),
+        pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
+        pybind11::arg("initial_normal") = pybind11::none());
+  m.def("apply_long", &apply_long, "reconstruct autograd apply for chains of any length", pybind11::arg("lengths"), pybind11::arg("angles"),
         pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
         pybind11::arg("initial_normal") = pybind11::none());
   m.def("torsion_apply", &torsion_apply, "torsion-only autograd apply", pybind11::arg("raw_pairs"), pybind11::arg("constants"));

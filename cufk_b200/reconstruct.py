@@ -55,3 +55,25 @@ def reconstruct(
     lengths, angles, dihedrals, single = _batched_inputs(lengths, angles, dihedrals)
     xyz = _C.apply(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
     return xyz[0] if single else xyz
+
+
+def reconstruct_long(
+    lengths: torch.Tensor,
+    angles: torch.Tensor,
+    dihedrals: torch.Tensor,
+    p0: torch.Tensor | None = None,
+    first_direction: torch.Tensor | None = None,
+    initial_normal: torch.Tensor | None = None,
+) -> torch.Tensor:
+    r"""``reconstruct`` for chains of any length N >= 4 (float32 and float64).
+
+    The reference stops at ``BLOCK_SCAN_MAX_POINT_COUNT`` points and leaves longer chains to a scan
+    it does not ship (README.md:52).  Here each chain is split into balanced segments of at most
+    2048 steps, one CTA each; the segments exchange their frame products through a workspace that
+    the wrapper allocates per call.  Arguments, shapes, anchors and gradients are those of
+    ``reconstruct``.  The backward needs an orthonormal base frame: a collinear first angle or
+    degenerate anchors give NaN gradients.
+    """
+    lengths, angles, dihedrals, single = _batched_inputs(lengths, angles, dihedrals)
+    xyz = _C.apply_long(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
+    return xyz[0] if single else xyz

@@ -65,7 +65,9 @@ enum cufkb_status {
   CUFKB_ERROR_BAD_STRIDE = 6,     /* torsion row stride too small for the pairs */
   CUFKB_ERROR_MISALIGNED = 7,     /* a pointer not aligned to its element size */
   CUFKB_ERROR_INVALID_VALUE = 8,  /* NULL torsion constants */
-  CUFKB_ERROR_CUDA = 9            /* a CUDA runtime error; see cufkb_last_cuda_error() */
+  CUFKB_ERROR_CUDA = 9,           /* a CUDA runtime error; see cufkb_last_cuda_error() */
+  CUFKB_ERROR_WORKSPACE = 10,     /* workspace smaller than cufkb_block_long_workspace_bytes */
+  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11 /* the long-chain path: float32 and float64 only */
 };
 
 /* Backbone constants of compile_torsion(bond_lengths, bond_angles).  Bond i is used by every
@@ -124,6 +126,26 @@ CUFKB_API int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, 
                                     const cufkb_torsion_constants* constants, const void* xyz, const void* grad_xyz,
                                     void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
                                     cufkb_stream_t stream);
+
+/* Chains of any length N >= 4 (no counterpart in the reference, which stops at
+ * BLOCK_SCAN_MAX_POINT_COUNT = 2051 points and leaves longer chains to a scan it does not ship,
+ * README.md:52).  A chain is split into balanced segments of at most 2048 steps, one CTA each;
+ * segments exchange their affine totals (and, backward, their force/moment sums) through a
+ * caller-provided device workspace of cufkb_block_long_workspace_bytes bytes (16-byte aligned,
+ * nothing needs to be initialised; one workspace serves one call at a time).  float32 and float64.
+ * Same arguments and results as cufkb_block_forward / cufkb_block_backward otherwise; the backward
+ * reads the forward's xyz and needs an orthonormal base frame (a collinear first angle or
+ * degenerate anchors give NaN gradients). */
+CUFKB_API int cufkb_block_long_workspace_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes);
+
+CUFKB_API int cufkb_block_forward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                             const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
+                             void* workspace, size_t workspace_bytes, cufkb_stream_t stream);
+
+CUFKB_API int cufkb_block_backward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                              const void* first_direction, const void* initial_normal, const void* xyz, const void* grad_xyz,
+                              void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
+                              void* workspace, size_t workspace_bytes, cufkb_stream_t stream);
 
 /* Static text for a status code. */
 CUFKB_API const char* cufkb_status_string(int status);

@@ -15,7 +15,8 @@ PKG = Path(cufk.__file__).resolve().parent
 
 
 def test_public_surface_matches_reference():
-    assert set(cufk.__all__) == {"BLOCK_SCAN_MAX_POINT_COUNT", "__version__", "compile_torsion", "reconstruct"}
+    # the reference's surface, plus reconstruct_long for chains the reference cannot reconstruct
+    assert set(cufk.__all__) == {"BLOCK_SCAN_MAX_POINT_COUNT", "__version__", "compile_torsion", "reconstruct", "reconstruct_long"}
     assert cufk.BLOCK_SCAN_MAX_POINT_COUNT == 2051
     assert cufk.__version__ == "0.1.0"
 
@@ -27,6 +28,8 @@ def test_host_tensors_are_rejected_with_reference_text():
         cufk.reconstruct(torch.ones(9), torch.ones(8), torch.ones(7))
     with pytest.raises(RuntimeError, match="raw_pairs must be CUDA"):
         cufk.compile_torsion((1.0, 1.0, 1.0), (2.0, 2.0, 2.0))(torch.ones(2, 8))
+    with pytest.raises(RuntimeError, match="lengths must be CUDA"):
+        cufk.reconstruct_long(torch.ones(2, 9), torch.ones(2, 8), torch.ones(2, 7))
 
 
 def test_compile_torsion_is_cached_per_constants():
