@@ -426,6 +426,30 @@ int check_long(int dtype, int64_t batch, int64_t points) {
   return CUFKB_SUCCESS;
 }
 
+// Scratch of cufkb_block_forward_long_static: a fixed device array, so that the call allocates
+// nothing.  It holds the segment totals only, written by the first kernel of a call before the
+// second reads them: nothing in it needs to start at zero or survive between calls.
+constexpr size_t kStaticScratchBytes = size_t(2) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct ScratchAddress {
+  std::once_flag once;
+  void* ptr = nullptr;
+  int error = 0;
+};
+ScratchAddress g_scratch_address[kMaxDevices];
+
+// The array's address on device `dev`, looked up once per device.
+void* static_scratch(int dev, int* error) {
+  ScratchAddress& a = g_scratch_address[dev];
+  std::call_once(a.once, [&] {
+    const cudaError_t e = cudaGetSymbolAddress(&a.ptr, g_static_scratch);
+    a.error = static_cast<int>(e);
+  });
+  *error = a.error;
+  return a.ptr;
+}
+
 }  // namespace
 
 namespace {
@@ -626,6 +650,26 @@ int cufkb_block_forward_long(int dtype, const void* lengths, const void* angles,
   return block_forward_long_impl<double>(a, xyz, batch, points, workspace, s);
 }
 
+int cufkb_block_forward_long_static(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                    const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
+                                    cufkb_stream_t stream) {
+  if (int st = check_long(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz}, {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz})) {
+    return st;
+  }
+  if (static_cast<size_t>(batch) * long_plan(points).segs * cufkb::kTotalWords * elem_size(dtype) > kStaticScratchBytes) {
+    return CUFKB_ERROR_SCRATCH_CAPACITY;
+  }
+  int dev = 0;
+  if (int e = current_device(&dev)) return fail_cuda(static_cast<cudaError_t>(e));
+  int err = 0;
+  void* scratch = static_scratch(dev, &err);
+  if (err != 0) return fail_cuda(static_cast<cudaError_t>(err));
+  return cufkb_block_forward_long(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, points, scratch,
+                                  kStaticScratchBytes, stream);
+}
+
 int cufkb_block_backward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                               const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
                               void* grad_dihedrals, int64_t batch, int64_t points, void* workspace, size_t workspace_bytes, cufkb_stream_t stream) {
@@ -676,6 +720,8 @@ const char* cufkb_status_string(int status) {
       return "workspace is smaller than cufkb_block_long_workspace_bytes";
     case CUFKB_ERROR_UNSUPPORTED_DTYPE:
       return "chains longer than 2051 points support float32 and float64";
+    case CUFKB_ERROR_SCRATCH_CAPACITY:
+      return "batch x segments exceeds the 2 MiB static scratch of cufkb_block_forward_long_static";
     default:
       return "unknown status";
   }

@@ -67,7 +67,8 @@ enum cufkb_status {
   CUFKB_ERROR_INVALID_VALUE = 8,  /* NULL torsion constants */
   CUFKB_ERROR_CUDA = 9,           /* a CUDA runtime error; see cufkb_last_cuda_error() */
   CUFKB_ERROR_WORKSPACE = 10,     /* workspace smaller than cufkb_block_long_workspace_bytes */
-  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11 /* the long-chain path: float32 and float64 only */
+  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11, /* the long-chain path: float32 and float64 only */
+  CUFKB_ERROR_SCRATCH_CAPACITY = 12   /* cufkb_block_forward_long_static: call too large for its scratch */
 };
 
 /* Backbone constants of compile_torsion(bond_lengths, bond_angles).  Bond i is used by every
@@ -141,6 +142,29 @@ CUFKB_API int cufkb_block_long_workspace_bytes(int dtype, int64_t batch, int64_t
 CUFKB_API int cufkb_block_forward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                              const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
                              void* workspace, size_t workspace_bytes, cufkb_stream_t stream);
+
+/* cufkb_block_forward_long for callers that cannot provide a workspace.  No counterpart in the
+ * reference.  It is meant for hosts that hold no device allocator of their own (a language binding
+ * that only passes on the pointers it was given) and for code that must not allocate on its path
+ * (a loop with a fixed device-memory budget).
+ *
+ * The call allocates nothing.  Its scratch is a file-scope static device array of 2 MiB inside
+ * libcufkb.so; the library looks up its address once per device, with cudaGetSymbolAddress, on the
+ * first call on that device.  Make that first call outside any stream capture (a plain warm-up
+ * call will do).  Nothing in the scratch needs to start at zero: each call writes the segment
+ * totals before reading them.
+ *
+ * Limits:
+ * - batch x segments x 12 x sizeof(element) must fit in 2 MiB, where
+ *   segments = ceil((points - 3) / 2048). For example, 4096 float32 chains of up to 20483 points.
+ *   Larger calls return CUFKB_ERROR_SCRATCH_CAPACITY and launch nothing.
+ * - The scratch is shared by every call on a device. Calls that overlap in time (on different
+ *   streams, or from different threads) race on it and can return wrong coordinates. Keep calls of
+ *   this entry point on one device in one stream, or use cufkb_block_forward_long with a workspace
+ *   per stream. */
+CUFKB_API int cufkb_block_forward_long_static(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                    const void* first_direction, const void* initial_normal, void* xyz, int64_t batch, int64_t points,
+                                    cufkb_stream_t stream);
 
 CUFKB_API int cufkb_block_backward_long(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                               const void* first_direction, const void* initial_normal, const void* xyz, const void* grad_xyz,

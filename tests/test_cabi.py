@@ -125,6 +125,25 @@ def test_torsion_from_xyz_validation(lib):
     assert lib.cufkb_torsion_backward_from_xyz(F64, 16, 14, ctypes.byref(c), 32, 64, 128, 14, 2, 2052, None) == TOO_MANY_STEPS
 
 
+def test_long_path_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_long_static.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_forward_long.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp, ctypes.c_size_t, vp]
+    lib.cufkb_block_long_workspace_bytes.argtypes = [ctypes.c_int, i64, i64, ctypes.POINTER(ctypes.c_size_t)]
+    size = ctypes.c_size_t()
+    assert lib.cufkb_block_long_workspace_bytes(F32, 4, 10000, ctypes.byref(size)) == SUCCESS
+    assert size.value == 4 * 5 * 18 * 4  # 9997 steps: 5 segments of at most 2048
+    assert lib.cufkb_block_long_workspace_bytes(F16, 4, 10000, ctypes.byref(size)) == 11
+    assert lib.cufkb_block_long_workspace_bytes(F32, 4, 3, ctypes.byref(size)) == POINT_COUNT
+    assert lib.cufkb_block_forward_long(F32, 16, 32, 48, None, None, None, 64, 2, 5000, None, 0, None) == NULL_POINTER
+    assert lib.cufkb_block_forward_long(F32, 16, 32, 48, None, None, None, 64, 2, 5000, 72, 10**6, None) == MISALIGNED
+    assert lib.cufkb_block_forward_long(F32, 16, 32, 48, None, None, None, 64, 2, 5000, 80, 16, None) == 10
+    assert lib.cufkb_block_forward_long_static(BF16, 16, 32, 48, None, None, None, 64, 2, 5000, None) == 11
+    assert lib.cufkb_block_forward_long_static(F32, 16, 32, 48, None, None, None, 64, 100, 10**6, None) == 12
+    assert lib.cufkb_block_forward_long_static(F32, 16, 32, 48, None, None, None, 64, 0, 5000, None) == SUCCESS
+    assert lib.cufkb_status_string(12).startswith(b"batch x segments exceeds")
+
+
 def test_status_strings(lib):
     assert lib.cufkb_status_string(SUCCESS) == b"success"
     assert lib.cufkb_status_string(POINT_COUNT) == b"point_count must be >= 4"
