@@ -574,13 +574,21 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
   ChainViews<T> cv;
   unsigned char* p = stage_block_inputs<T>(cv, smem, args, chain, N, 0, tid, nthr);
   cv.G = stage_row_async(p, grow, 3 * N, tid, nthr);
-  const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+  // thread 0 builds the first frame from global memory while the rows stage; every thread reads it
+  // from shared memory
+  __shared__ FirstFrame<V> first;
+  if (tid == 0) {
+    const AnchorFrame<R> af0 = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+    const V l0 = to_r<V>(args.lengths[chain * (N - 1)]);
+    const V l1 = to_r<V>(args.lengths[chain * (N - 1) + 1]);
+    const V a0 = to_r<V>(args.angles[chain * (N - 2)]);
+    first = FirstFrame<V>{af0, backward_frame<V>(af0, l0, l1, a0)};
+  }
   cp_async_wait_all();
   __syncthreads();
 
-  V l0, l1, a0;
-  first_inputs(cv, l0, l1, a0);
-  const BackwardFrame<V> bf = backward_frame<V>(af, l0, l1, a0);
+  const AnchorFrame<V>& af = first.af;
+  const BackwardFrame<V>& bf = first.bf;
   auto step = [&](int s) {
     V l, th, ph, st, ct, sp, cp;
     block_step_inputs<T>(cv, s, l, th, ph);
