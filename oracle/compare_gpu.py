@@ -8,6 +8,7 @@ forward plus ``backward`` of a fixed grad.  Inputs are device-resident; several 
 so that each step reads from HBM; CUDA events around ``--reps`` steps after warm-up.
 
     python oracle/compare_gpu.py [--reps 50] > compare.json
+    python oracle/compare_gpu.py --accuracy > accuracy.json   # errors against float64
 """
 
 from __future__ import annotations
@@ -107,12 +108,42 @@ def torsion_case(batch, points, dtype, reps):
     return out
 
 
+def _errors(fn, inp, dtype, anchors):
+    """max-abs xyz error and worst gradient relative-L2 error against the float64 oracle, for inputs
+    cast to `dtype` (the oracle sees the same rounded inputs)."""
+    L, A, D = (inp[k].to("cuda", dtype).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    kw = {k: inp[k].to("cuda", dtype) for k in ANCHOR_KEYS} if anchors else {}
+    xyz = fn(L, A, D, **kw)
+    xyz.backward(inp["grad"].to("cuda", dtype))
+    c = {k: v.to(dtype).double() for k, v in inp.items()}
+    ref = nerf64.reconstruct64_with_grads(c["lengths"], c["angles"], c["dihedrals"], c["grad"], **({k: c[k] for k in ANCHOR_KEYS} if anchors else {}))
+    xerr = float((xyz.detach().double().cpu() - ref[0]).abs().max())
+    gerr = max(float((g.double().cpu() - r).norm() / r.norm()) for g, r in zip((L.grad, A.grad, D.grad), ref[1:]))
+    return {"xyz_max_abs": xerr, "grad_rel_l2": gerr}
+
+
+def accuracy() -> dict:
+    out = {}
+    for name, batch, points, dtype, anchors in (
+        ("config2 fp32 B=16 N=2051 anchors", 16, 2051, torch.float32, True),
+        ("config4 fp16 B=64 N=1026", 64, 1026, torch.float16, False),
+        ("config4 bf16 B=64 N=1026", 64, 1026, torch.bfloat16, False),
+    ):
+        inp = nerf64.make_inputs(batch, points, seed=points, anchors=anchors)
+        out[name] = {"reference": _errors(ref_kernels.ref_reconstruct, inp, dtype, anchors), "cufk_b200": _errors(cufk.reconstruct, inp, dtype, anchors)}
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--accuracy", action="store_true", help="errors against float64 instead of timings")
     args = ap.parse_args()
     if not (ref_kernels.available("block") and ref_kernels.available("torsion")):
         raise SystemExit("reference kernels not built (python oracle/build_ref.py)")
+    if args.accuracy:
+        print(json.dumps(accuracy(), indent=1))
+        return
     r = args.reps
     res = {
         "config0 block B=64 N=384 fp32": block_case(64, 384, torch.float32, False, r),
