@@ -659,38 +659,43 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const bool general = first.bf.general;  // uniform over the CTA
   bool redo = general;
   if (!redo) {
-    // moments about o = p2 (the chain's own origin, atom 2 of the forward's xyz): tau then loses no
-    // precision to the chain's distance from the world origin
+    // moments about o = p2 (the chain's own origin, atom 2 of the forward's xyz): the sums then lose
+    // no precision to the chain's distance from the world origin
     const V o[3] = {cv.pos(6), cv.pos(7), cv.pos(8)};
     V gsum[3] = {V(0), V(0), V(0)};
     V msum[3] = {V(0), V(0), V(0)};
     V xmax2 = V(0);  // largest |x|^2 of the thread's atoms (world), for the short-bond test
-    int off = 3 * (range.first + 3);
+    {
+      const T* px = cv.Y + 3 * (range.first + 3);
+      const T* pg = cv.G + 3 * (range.first + 3);
 #pragma unroll 4
-    for (int k = 0; k < range.count; ++k, off += 3) {
-      const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
-      const V xw[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
-      xmax2 = fmax(xmax2, dot3(xw, xw));
-      const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
-      V mx[3];
-      cross3(x, g, mx);
+      for (int k = 0; k < range.count; ++k, px += 3, pg += 3) {
+        const V g[3] = {to_r<V>(pg[0]), to_r<V>(pg[1]), to_r<V>(pg[2])};
+        const V xw[3] = {to_r<V>(px[0]), to_r<V>(px[1]), to_r<V>(px[2])};
+        xmax2 = fmax(xmax2, dot3(xw, xw));
+        const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
+        V mx[3];
+        cross3(x, g, mx);
 #pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        gsum[i] = vadd(gsum[i], g[i]);
-        msum[i] = vadd(msum[i], mx[i]);
+        for (int i = 0; i < 3; ++i) {
+          gsum[i] = vadd(gsum[i], g[i]);
+          msum[i] = vadd(msum[i], mx[i]);
+        }
       }
     }
     V Fs[3], Ms[3];
     suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
     const V F3[3] = {Fs[0], Fs[1], Fs[2]};
     const V M3[3] = {Ms[0], Ms[1], Ms[2]};
-    // sweep: x2 = x_{s+2} (world), up = u_{s+1} carried from step to step.  Threads without steps
-    // read nothing (their first step lies past the chain).
+    // sweep: x2 = x_{s+2} (world), up = u_{s+1}, tau = tau_s = sum_{j >= s+3} (x_j - x_{s+2}) x g_j,
+    // carried from step to step as tau_{s+1} = tau_s - (x_{s+3} - x_{s+2}) x F_s.  Threads without
+    // steps read nothing (their first step lies past the chain).
     V x2[3] = {V(0), V(0), V(0)};
     V up[3] = {V(0), V(0), V(0)};
+    V tau[3] = {V(0), V(0), V(0)};
     V dmin2 = V(0);
     if (range.count > 0) {
-      off = 3 * (range.first + 1);  // atoms first+1 and first+2 <= N-2
+      const int off = 3 * (range.first + 1);  // atoms first+1 and first+2 <= N-2
 #pragma unroll
       for (int i = 0; i < 3; ++i) x2[i] = cv.pos(off + 3 + i);
       const V d[3] = {vsub(x2[0], cv.pos(off)), vsub(x2[1], cv.pos(off + 1)), vsub(x2[2], cv.pos(off + 2))};
@@ -699,42 +704,46 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
       const V inv = vrsqrt(dmin2);
 #pragma unroll
       for (int i = 0; i < 3; ++i) up[i] = vmul(d[i], inv);
-    }
-    V wmin2 = V(1);
-    off = 3 * (range.first + 3);
-#pragma unroll 2
-    for (int k = 0; k < range.count; ++k, off += 3) {
-      const V x3[3] = {cv.pos(off), cv.pos(off + 1), cv.pos(off + 2)};
-      const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
-      const V d[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
-      const V d2 = dot3(d, d);
-      dmin2 = fmin(dmin2, d2);
-      const V inv = vrsqrt(d2);
-      const V uc[3] = {vmul(d[0], inv), vmul(d[1], inv), vmul(d[2], inv)};
       const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
       V xf[3];
       cross3(xr, Fs, xf);
-      const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
-      V w[3];
-      cross3(up, uc, w);
-      const V w2 = dot3(w, w);
-      wmin2 = fmin(wmin2, w2);
-      const V d_phi = dot3(up, tau);
-      const V d_len = dot3(uc, Fs);
-      const V d_theta = vneg(vmul(dot3(w, tau), vrsqrt(w2)));
-      const V x3r[3] = {vsub(x3[0], o[0]), vsub(x3[1], o[1]), vsub(x3[2], o[2])};
-      V mx[3];
-      cross3(x3r, g, mx);
 #pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        Fs[i] = vsub(Fs[i], g[i]);
-        Ms[i] = vsub(Ms[i], mx[i]);
-        x2[i] = x3[i];
-        up[i] = uc[i];
+      for (int i = 0; i < 3; ++i) tau[i] = vsub(Ms[i], xf[i]);
+    }
+    V wmin2 = V(1);
+    {
+      const T* px = cv.Y + 3 * (range.first + 3);
+      T* pg = cv.G + 3 * (range.first + 3);
+#pragma unroll 2
+      for (int k = 0; k < range.count; ++k, px += 3, pg += 3) {
+        const V x3[3] = {to_r<V>(px[0]), to_r<V>(px[1]), to_r<V>(px[2])};
+        const V g[3] = {to_r<V>(pg[0]), to_r<V>(pg[1]), to_r<V>(pg[2])};
+        const V d[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+        const V d2 = dot3(d, d);
+        dmin2 = fmin(dmin2, d2);
+        const V inv = vrsqrt(d2);
+        const V uc[3] = {vmul(d[0], inv), vmul(d[1], inv), vmul(d[2], inv)};
+        V w[3];
+        cross3(up, uc, w);
+        const V w2 = dot3(w, w);
+        wmin2 = fmin(wmin2, w2);
+        const V d_phi = dot3(up, tau);
+        const V d_len = dot3(uc, Fs);
+        const V d_theta = vneg(vmul(dot3(w, tau), vrsqrt(w2)));
+        // tau -= d x Fs, then Fs -= g
+        tau[0] = vfma(d[2], Fs[1], vfma(vneg(d[1]), Fs[2], tau[0]));
+        tau[1] = vfma(d[0], Fs[2], vfma(vneg(d[2]), Fs[0], tau[1]));
+        tau[2] = vfma(d[1], Fs[0], vfma(vneg(d[0]), Fs[1], tau[2]));
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          Fs[i] = vsub(Fs[i], g[i]);
+          x2[i] = x3[i];
+          up[i] = uc[i];
+        }
+        pg[0] = from_r<T>(d_len);
+        pg[1] = from_r<T>(d_theta);
+        pg[2] = from_r<T>(d_phi);
       }
-      cv.set_slot(off, d_len);
-      cv.set_slot(off + 1, d_theta);
-      cv.set_slot(off + 2, d_phi);
     }
     // Positions are accurate to ~1 ulp of |x|, so a bond direction from them is good to
     // ~ulp(|x|) / |d|: bonds shorter than 1e-3 |x|max, a plane normal with sin^2 < 1e-2 (and any
