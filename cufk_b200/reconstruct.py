@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from . import anchors
 from ._native import _C
 
 BLOCK_SCAN_MAX_POINT_COUNT = 2051
@@ -33,6 +34,8 @@ def reconstruct(
     p0: torch.Tensor | None = None,
     first_direction: torch.Tensor | None = None,
     initial_normal: torch.Tensor | None = None,
+    *,
+    anchor_grads: bool = False,
 ) -> torch.Tensor:
     r"""Reconstruct Cartesian coordinates from full internal coordinates.
 
@@ -49,11 +52,17 @@ def reconstruct(
 
     Notes:
         Inputs are CUDA tensors of one dtype among float16, bfloat16, float32 and float64, with
-        4 <= N <= 2051.  Gradients flow to lengths, angles and dihedrals; anchors take none.
-        16-bit inputs are computed in float32 and rounded once on output.
+        4 <= N <= 2051.  Gradients flow to lengths, angles and dihedrals.  Anchors take none and an
+        anchor that requires grad raises, as in the reference, unless ``anchor_grads=True`` (an
+        extension the reference does not have, see ``anchors.py``): then anchors that require
+        grad receive theirs.  16-bit inputs are computed in float32 and rounded once on output.
     """
     lengths, angles, dihedrals, single = _batched_inputs(lengths, angles, dihedrals)
-    xyz = _C.apply(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
+    lengths, angles, dihedrals = lengths.contiguous(), angles.contiguous(), dihedrals.contiguous()
+    if anchor_grads and any(a is not None and a.requires_grad for a in (p0, first_direction, initial_normal)):
+        xyz = anchors.AnchorGradReconstruct.apply(lengths, angles, dihedrals, p0, first_direction, initial_normal)
+    else:
+        xyz = _C.apply(lengths, angles, dihedrals, p0, first_direction, initial_normal)
     return xyz[0] if single else xyz
 
 

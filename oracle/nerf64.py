@@ -173,6 +173,20 @@ def reconstruct64_with_grads(lengths, angles, dihedrals, grad_xyz, p0=None, firs
     return xyz.detach(), gl, ga, gd
 
 
+def reconstruct64_anchor_grads(lengths, angles, dihedrals, grad_xyz, p0, first_direction, initial_normal):
+    """Gradients of <grad_xyz, xyz> with respect to the three anchors, by float64 autograd through
+    the whole restated forward (first frame block.cu:113-148 and the chain block.cu:157-204).
+    The reference itself rejects anchor gradients (extension_utils.cuh:81); this is the check for
+    the extension that provides them.  Returns (xyz, d p0, d first_direction, d initial_normal)."""
+    L, A, D = (x.detach().to(F64) for x in (lengths, angles, dihedrals))
+    anchors = [x.detach().to("cpu", F64).requires_grad_(True) for x in (p0, first_direction, initial_normal)]
+    xyz = nerf64_sincos(L[:, 2:], torch.sin(A[:, 1:]), torch.cos(A[:, 1:]), torch.sin(D), torch.cos(D), L[:, 0], L[:, 1], A[:, 0], *anchors)
+    grads = torch.autograd.grad((xyz * grad_xyz.detach().to(F64)).sum(), anchors, allow_unused=True)
+    # an anchor the frame does not use (the initial normal when it is parallel to the first
+    # direction) has a zero gradient
+    return (xyz.detach(), *(torch.zeros(3, dtype=F64) if gr is None else gr for gr in grads))
+
+
 def block_backward64(lengths, angles, dihedrals, grad_xyz, p0=None, first_direction=None, initial_normal=None):
     """The reference's explicit backward formulas, restated in float64 (batched inputs only).
 
