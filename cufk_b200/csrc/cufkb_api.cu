@@ -36,6 +36,11 @@ constexpr int kMinItems = 5;      // never split a chain below this many steps p
 #endif
 constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;
 constexpr int kXyzTargetWarpsPerSm = CUFKB_XYZ_TARGET_WARPS_PER_SM;
+// Warps per SM the block forward's grid must offer before a small batch stops splitting its chains
+// over more warps.  Each extra warp adds scan work; on B200 at N=768 two warps per chain beat three
+// to five at 1024 and 2048 chains, and four match them at 512 (per-launch times 12.3 vs 14.3 us and
+// 17.0 vs 18.4 us).
+constexpr int kForwardFillWarpsPerSm = 12;
 
 struct DeviceCache {
   std::once_flag once;
@@ -131,10 +136,10 @@ int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
 // Warps per chain (W) and steps per thread (K).  A chain needs W >= ceil(steps / (32 kTargetItems))
 // so that a thread walks at most ~kTargetItems steps.  Beyond that, W grows while the SM would hold
-// fewer than kTargetWarpsPerSm resident warps (shared memory per chain and registers per thread
-// bound the resident chains), and while the whole grid offers fewer than that many warps per SM
-// (small batches), as long as a thread keeps >= kMinItems steps.  K is made odd so that the
-// threads' slot strides (3K words) fall on 32 distinct shared-memory banks.
+// fewer than `target` resident warps (shared memory per chain and registers per thread bound the
+// resident chains), and while the whole grid offers fewer than `fill` warps per SM (small
+// batches), as long as a thread keeps >= kMinItems steps.  K is made odd so that the threads' slot
+// strides (3K words) fall on 32 distinct shared-memory banks.
 struct Plan {
   int threads;
   int items;
@@ -151,7 +156,7 @@ int resident_warps(const DeviceCache& d, const KernelCache& k, size_t dyn_smem, 
   return chains * warps;
 }
 
-Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCache& k, size_t dyn_smem, int target) {
+Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCache& k, size_t dyn_smem, int target, int fill) {
   const int steps = points - 3;
   int warps = ceil_div(steps, cufkb::kWarp * kTargetItems);
   if (warps < 1) warps = 1;
@@ -161,7 +166,7 @@ Plan make_plan(int64_t batch, int points, const DeviceCache& d, const KernelCach
          resident_warps(d, k, dyn_smem, warps + 1) > resident_warps(d, k, dyn_smem, warps)) {
     ++warps;
   }
-  const int64_t grid_target = int64_t(d.sm_count) * target;
+  const int64_t grid_target = int64_t(d.sm_count) * fill;
   while (splittable(warps) && batch * warps < grid_target) ++warps;
   int items = ceil_div(steps, cufkb::kWarp * warps);
   if ((items & 1) == 0) ++items;
@@ -201,7 +206,8 @@ struct LaunchEnv {
 
 // Device, kernel footprint, shared-memory opt-in and plan of one launch.
 template <typename Kernel>
-int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem, int target = kTargetWarpsPerSm) {
+int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem, int target = kTargetWarpsPerSm,
+               int fill = 0) {
   const int e = current_device(&env->dev);
   if (e != 0) return fail_cuda(static_cast<cudaError_t>(e));
   env->cache = device_cache(env->dev);
@@ -210,7 +216,7 @@ int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int 
   if (k->error != 0) return fail_cuda(static_cast<cudaError_t>(k->error));
   if (static_cast<int>(smem) + k->static_smem > env->cache->max_smem_optin) return fail_cuda(cudaErrorInvalidValue);
   if (cudaError_t err = ensure_smem_limit(kernel, &g_kernels[kernel_id], env->dev, env->cache->max_smem_optin)) return fail_cuda(err);
-  env->plan = make_plan(batch, points, *env->cache, *k, smem, target);
+  env->plan = make_plan(batch, points, *env->cache, *k, smem, target, fill > 0 ? fill : target);
   return CUFKB_SUCCESS;
 }
 
@@ -243,7 +249,9 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kBlockForward, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockForward, dtype_index<T>()), batch, points, smem, kTargetWarpsPerSm, kForwardFillWarpsPerSm)) {
+    return st;
+  }
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
