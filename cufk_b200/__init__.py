@@ -3,11 +3,12 @@
 ``import cufk_b200 as cufk`` gives the reference's public surface (src/cufk/__init__.py:1-11):
 ``reconstruct``, ``compile_torsion``, ``BLOCK_SCAN_MAX_POINT_COUNT`` and ``__version__``; and
 ``reconstruct_long`` for chains longer than ``BLOCK_SCAN_MAX_POINT_COUNT``, which the reference
-does not support; and ``ops``, the same path as ``torch.library`` operators
+does not support; ``reconstruct_packed`` for ragged batches (chains of different lengths, packed);
+and ``ops``, the same path as ``torch.library`` operators
 (``torch.ops.cufk_b200.*``) that ``torch.compile`` traces through.
 """
 
-from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct, reconstruct_long
+from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct, reconstruct_long, reconstruct_packed
 from .torsion import compile_torsion
 from . import ops  # noqa: E402  (registers the torch.library operators)
 
@@ -20,4 +21,5 @@ __all__ = [
     "ops",
     "reconstruct",
     "reconstruct_long",
+    "reconstruct_packed",
 ]

@@ -245,7 +245,7 @@ constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 template <typename T>
 int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const int64_t* offsets = nullptr) {
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
@@ -254,7 +254,7 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   }
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
@@ -262,14 +262,14 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
 
 template <typename T>
 int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL, void* gA,
-                        void* gD, int64_t batch, int points, cudaStream_t stream) {
+                        void* gD, int64_t batch, int points, cudaStream_t stream, const int64_t* offsets = nullptr) {
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kBlockBackward, dtype_index<T>()), batch, points, smem)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
                                                                           static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
@@ -279,14 +279,14 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
 // Backward from the forward's xyz (32- and 64-bit types).
 template <typename T>
 int block_backward_xyz_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
-                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
+                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, const int64_t* offsets = nullptr) {
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_xyz_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardXyz, dtype_index<T>()), batch, points, smem, kXyzTargetWarpsPerSm)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
                                                                           static_cast<T*>(gA), static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
@@ -473,23 +473,88 @@ int check_block_pointers(int dtype, std::initializer_list<const void*> required,
   return CUFKB_SUCCESS;
 }
 
+// Packed batches: the offsets array (B+1 int64) must be given, 8-byte aligned.
+int check_offsets(const int64_t* offsets, bool packed) {
+  if (!packed) return CUFKB_SUCCESS;
+  if (!offsets) return CUFKB_ERROR_NULL_POINTER;
+  return aligned(offsets, alignof(int64_t)) ? CUFKB_SUCCESS : CUFKB_ERROR_MISALIGNED;
+}
+
 int block_forward_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
-                           int64_t points, cufkb_stream_t stream) {
+                           int64_t points, cufkb_stream_t stream, bool packed = false, const int64_t* offsets = nullptr) {
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
   if (int st = check_block_pointers(dtype, {L, A, D, xyz}, {L, A, D, p0, fd, nn, xyz})) return st;
+  if (int st = check_offsets(offsets, packed)) return st;
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, batch, n, s);
+      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
     case CUFKB_FLOAT64:
-      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, batch, n, s);
+      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
     case CUFKB_FLOAT16:
-      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s);
+      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
     default:
-      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s);
+      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
   }
+}
+
+int block_backward_dispatch(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                            const void* initial_normal, const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                            int64_t points, cufkb_stream_t stream, bool packed = false, const int64_t* offsets = nullptr) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
+  }
+  if (int st = check_offsets(offsets, packed)) return st;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CUFKB_FLOAT32:
+      return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                        grad_dihedrals, batch, n, s, offsets);
+    case CUFKB_FLOAT64:
+      return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s, offsets);
+    case CUFKB_FLOAT16:
+      return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s, offsets);
+    default:
+      return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                                grad_dihedrals, batch, n, s, offsets);
+  }
+}
+
+int block_backward_from_xyz_dispatch(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                                     const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
+                                     void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream, bool packed = false,
+                                     const int64_t* offsets = nullptr) {
+  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
+    if (int st = check_shape(dtype, batch, points)) return st;
+    if (batch > 0 && !xyz) return CUFKB_ERROR_NULL_POINTER;
+    return block_backward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                   grad_dihedrals, batch, points, stream, packed, offsets);
+  }
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
+  }
+  if (int st = check_offsets(offsets, packed)) return st;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    return block_backward_xyz_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                          grad_dihedrals, batch, n, s, offsets);
+  }
+  return block_backward_xyz_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
+                                         grad_dihedrals, batch, n, s, offsets);
 }
 
 }  // namespace
@@ -506,55 +571,30 @@ int cufkb_block_forward(int dtype, const void* lengths, const void* angles, cons
 int cufkb_block_backward(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                          const void* initial_normal, const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
                          int64_t points, cufkb_stream_t stream) {
-  if (int st = check_shape(dtype, batch, points)) return st;
-  if (batch == 0) return CUFKB_SUCCESS;
-  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
-                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                     grad_dihedrals})) {
-    return st;
-  }
-  const int n = static_cast<int>(points);
-  auto s = reinterpret_cast<cudaStream_t>(stream);
-  switch (dtype) {
-    case CUFKB_FLOAT32:
-      return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                        grad_dihedrals, batch, n, s);
-    case CUFKB_FLOAT64:
-      return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s);
-    case CUFKB_FLOAT16:
-      return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s);
-    default:
-      return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                                grad_dihedrals, batch, n, s);
-  }
+  return block_backward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
+                                 grad_dihedrals, batch, points, stream);
 }
 
 int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                                   const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
                                   void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream) {
-  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
-    if (int st = check_shape(dtype, batch, points)) return st;
-    if (batch > 0 && !xyz) return CUFKB_ERROR_NULL_POINTER;
-    return cufkb_block_backward(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                grad_dihedrals, batch, points, stream);
-  }
-  if (int st = check_shape(dtype, batch, points)) return st;
-  if (batch == 0) return CUFKB_SUCCESS;
-  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, xyz, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
-                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
-                                     grad_dihedrals})) {
-    return st;
-  }
-  const int n = static_cast<int>(points);
-  auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == CUFKB_FLOAT32) {
-    return block_backward_xyz_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
-                                          grad_dihedrals, batch, n, s);
-  }
-  return block_backward_xyz_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s);
+  return block_backward_from_xyz_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths,
+                                          grad_angles, grad_dihedrals, batch, points, stream);
+}
+
+int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                               const void* initial_normal, const int64_t* chain_points, void* xyz, int64_t batch, int64_t max_points,
+                               cufkb_stream_t stream) {
+  return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, max_points, stream, true,
+                                chain_points);
+}
+
+int cufkb_block_backward_packed_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                         const void* first_direction, const void* initial_normal, const int64_t* chain_points, const void* xyz,
+                                         const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                                         int64_t max_points, cufkb_stream_t stream) {
+  return block_backward_from_xyz_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths,
+                                          grad_angles, grad_dihedrals, batch, max_points, stream, true, chain_points);
 }
 
 int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,

@@ -527,9 +527,33 @@ __device__ __forceinline__ ChainFrame<V> chain_frame(const AnchorFrame<typename 
 // ------------------------------------------------------------------------------------------
 struct ChainGeometry {
   int batch;   // B
-  int points;  // N
+  int points;  // N (a packed batch: the largest N of its chains)
   int steps;   // N - 3
   int items;   // K: steps per thread (odd)
+  // Packed (ragged) batch: chain b's points are [offsets[b], offsets[b+1]) of the packed xyz; null
+  // for a (B, N) batch.
+  const int64_t* offsets = nullptr;
 };
+
+// Element offsets of one chain's rows in the (B, N-1), (B, N-2), (B, N-3) and (B, N, 3) arrays,
+// or in their packed forms, where chain b with points [p, p + N_b) owns lengths [p - b, p - b +
+// N_b - 1), angles [p - 2b, ...), dihedrals [p - 3b, ...) and xyz rows [p, p + N_b).
+struct ChainRows {
+  int points;  // N of this chain
+  int64_t lengths, angles, dihedrals, xyz;
+};
+
+__host__ __device__ inline ChainRows rows_at(int64_t chain, int64_t first_point, int points) {
+  return {points, first_point - chain, first_point - 2 * chain, first_point - 3 * chain, 3 * first_point};
+}
+
+// A packed chain whose point count lies outside [4, geo.points] gets points = 0 (the kernels leave
+// it untouched).
+__device__ __forceinline__ ChainRows chain_rows(const ChainGeometry& g, int64_t chain) {
+  if (g.offsets == nullptr) return rows_at(chain, chain * g.points, g.points);
+  const int64_t p0 = g.offsets[chain];
+  const int64_t n = g.offsets[chain + 1] - p0;
+  return rows_at(chain, p0, (n >= 4 && n <= g.points) ? static_cast<int>(n) : 0);
+}
 
 }  // namespace cufkb

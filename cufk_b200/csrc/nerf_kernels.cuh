@@ -68,10 +68,10 @@ struct CtaExchange {
 // The chain's first frame from its anchors and (lengths[0], lengths[1], angles[0]), read from
 // global memory (one thread per CTA builds it; the staged rows are still in flight).
 template <typename T, typename V>
-__device__ __forceinline__ ChainFrame<V> chain_frame_of(const BlockArgs<T>& args, const AnchorFrame<V>& af, int64_t chain, int N) {
-  const V l0 = to_r<V>(args.lengths[chain * (N - 1)]);
-  const V l1 = to_r<V>(args.lengths[chain * (N - 1) + 1]);
-  const V a0 = to_r<V>(args.angles[chain * (N - 2)]);
+__device__ __forceinline__ ChainFrame<V> chain_frame_of(const BlockArgs<T>& args, const AnchorFrame<V>& af, const ChainRows& rows) {
+  const V l0 = to_r<V>(args.lengths[rows.lengths]);
+  const V l1 = to_r<V>(args.lengths[rows.lengths + 1]);
+  const V a0 = to_r<V>(args.angles[rows.angles]);
   return chain_frame<V>(af, l0, l1, a0);
 }
 
@@ -167,12 +167,13 @@ __device__ __forceinline__ void scatter_block_inputs(T* X, const T* Lr, const T*
 // Stages a chain's inputs: scattered into the slots (4/8-byte types) or as rows (16-bit types, whose
 // slots hold float results).  Returns the first free byte after the chain's input region.
 template <typename T>
-__device__ __forceinline__ unsigned char* stage_block_inputs(ChainViews<T>& cv, unsigned char* smem, const BlockArgs<T>& args, int64_t chain, int N,
+__device__ __forceinline__ unsigned char* stage_block_inputs(ChainViews<T>& cv, unsigned char* smem, const BlockArgs<T>& args, const ChainRows& rows,
                                                              uintptr_t slot_residue, int tid, int nthr) {
   using R = typename ComputeOf<T>::type;
-  const T* Lr = args.lengths + chain * (N - 1);
-  const T* Ar = args.angles + chain * (N - 2);
-  const T* Dr = args.dihedrals + chain * (N - 3);
+  const int N = rows.points;
+  const T* Lr = args.lengths + rows.lengths;
+  const T* Ar = args.angles + rows.angles;
+  const T* Dr = args.dihedrals + rows.dihedrals;
   cv.X = reinterpret_cast<R*>(smem + slot_residue);
   unsigned char* p = smem + slot_bytes(N, sizeof(R));
   if constexpr (sizeof(T) >= 4) {
@@ -487,12 +488,13 @@ __device__ __forceinline__ void block_backward_general(const ChainViews<T>& cv, 
 }
 
 template <typename T>
-__device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* grad_lengths, T* grad_angles, T* grad_dihedrals, int64_t chain, int N, int tid,
+__device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* grad_lengths, T* grad_angles, T* grad_dihedrals, const ChainRows& rows, int tid,
                                                   int nthr) {
   using R = typename ComputeOf<T>::type;
-  T* gl = grad_lengths + chain * (N - 1);
-  T* ga = grad_angles + chain * (N - 2);
-  T* gd = grad_dihedrals + chain * (N - 3);
+  const int N = rows.points;
+  T* gl = grad_lengths + rows.lengths;
+  T* ga = grad_angles + rows.angles;
+  T* gd = grad_dihedrals + rows.dihedrals;
   const R* X = cv.X;
 #pragma unroll 2
   for (int i = tid; i < N - 1; i += nthr) {
@@ -515,17 +517,19 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
-  const int N = geo.points, St = geo.steps, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   const int64_t chain = blockIdx.x;
-  T* out = xyz + chain * 3 * N;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, St = N - 3, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  T* out = xyz + rows.xyz;
   ChainViews<T> cv;
-  stage_block_inputs<T>(cv, smem, args, chain, N, kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : 0, tid, nthr);
+  stage_block_inputs<T>(cv, smem, args, rows, kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : 0, tid, nthr);
   // thread 0 builds the first frame while the rows stage; the others read (F, p2) after the scan
   V first_points[9];
   if (tid == 0) {
     const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-    const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, chain, N);
+    const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, rows);
 #pragma unroll
     for (int i = 0; i < 9; ++i) ex.frame[i] = ff.F[i];
 #pragma unroll
@@ -567,21 +571,23 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
-  const int N = geo.points, St = geo.steps, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   const int64_t chain = blockIdx.x;
-  const T* grow = grad_xyz + chain * 3 * N;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, St = N - 3, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const T* grow = grad_xyz + rows.xyz;
   ChainViews<T> cv;
-  unsigned char* p = stage_block_inputs<T>(cv, smem, args, chain, N, 0, tid, nthr);
+  unsigned char* p = stage_block_inputs<T>(cv, smem, args, rows, 0, tid, nthr);
   cv.G = stage_row_async(p, grow, 3 * N, tid, nthr);
   // thread 0 builds the first frame from global memory while the rows stage; every thread reads it
   // from shared memory
   __shared__ FirstFrame<V> first;
   if (tid == 0) {
     const AnchorFrame<R> af0 = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-    const V l0 = to_r<V>(args.lengths[chain * (N - 1)]);
-    const V l1 = to_r<V>(args.lengths[chain * (N - 1) + 1]);
-    const V a0 = to_r<V>(args.angles[chain * (N - 2)]);
+    const V l0 = to_r<V>(args.lengths[rows.lengths]);
+    const V l1 = to_r<V>(args.lengths[rows.lengths + 1]);
+    const V a0 = to_r<V>(args.angles[rows.angles]);
     first = FirstFrame<V>{af0, backward_frame<V>(af0, l0, l1, a0)};
   }
   cp_async_wait_all();
@@ -602,7 +608,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
     block_backward_recompute<true, T, V>(cv, ex, af, bf, grow, range, nwarps, step);
   }
   __syncthreads();
-  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);
+  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, tid, nthr);
 }
 
 // Backward from the forward's xyz (4- and 8-byte types, base frame orthonormal).  In world
@@ -629,23 +635,25 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ CtaExchange<V> ex;
 
-  const int N = geo.points, St = geo.steps, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   const int64_t chain = blockIdx.x;
-  const T* grow = grad_xyz + chain * 3 * N;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, St = N - 3, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const T* grow = grad_xyz + rows.xyz;
   unsigned char* const slot_region = smem;
   unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
   ChainViews<T> cv;
-  cv.Y = stage_row_async(slot_region, xyz + chain * 3 * N, 3 * N, tid, nthr);
+  cv.Y = stage_row_async(slot_region, xyz + rows.xyz, 3 * N, tid, nthr);
   cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
   cv.X = cv.G;  // gradients go over the consumed grad row
   // thread 0 classifies the base frame while the rows stage; the first frame itself is only needed
   // again by thread 0 for the first-frame gradients (and by the recompute form)
   auto first_frame = [&]() {
     const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-    const R l0 = to_r<R>(args.lengths[chain * (N - 1)]);
-    const R l1 = to_r<R>(args.lengths[chain * (N - 1) + 1]);
-    const R a0 = to_r<R>(args.angles[chain * (N - 2)]);
+    const R l0 = to_r<R>(args.lengths[rows.lengths]);
+    const R l1 = to_r<R>(args.lengths[rows.lengths + 1]);
+    const R a0 = to_r<R>(args.angles[rows.angles]);
     return FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
   };
   // thread 0 builds the first frame while the rows stage and keeps it in shared memory for the
@@ -758,7 +766,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     const BackwardFrame<V>& bf = first.bf;
     // recompute form, laid out as in block_backward_kernel: inputs into the slots, grad row restaged
     __syncthreads();
-    stage_block_inputs<T>(cv, slot_region, args, chain, N, 0, tid, nthr);
+    stage_block_inputs<T>(cv, slot_region, args, rows, 0, tid, nthr);
     cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
     cp_async_wait_all();
     __syncthreads();
@@ -775,7 +783,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     }
   }
   __syncthreads();
-  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, chain, N, tid, nthr);
+  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, tid, nthr);
 }
 
 // --------------------------------------------------------------------------------------------

@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   V first_points[9];
   if (tid == 0) {
     const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-    const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, sg.chain, N);
+    const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, rows_at(sg.chain, sg.chain * N, N));
     const Affine<V> W = segment_carry<V>(totals + sg.chain * geo.segs * kTotalWords, sg.g, ff.F, ff.p2);
 #pragma unroll
     for (int i = 0; i < 9; ++i) ex.frame[i] = W.m[i];

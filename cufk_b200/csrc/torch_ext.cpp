@@ -289,6 +289,96 @@ Tensor apply_autograd(const Tensor& lengths, const Tensor& angles, const Tensor&
   return ReconstructAutograd::apply(lengths, angles, dihedrals, p0, first_direction, initial_normal);
 }
 
+// ---- packed (ragged) batches: chains of different lengths in one call (no counterpart in the
+// reference).  lengths/angles/dihedrals are 1-D packed rows, chain_points the (B+1,) int64 point
+// offsets on the device; the point total follows from the sizes (lengths has total - B entries), so
+// nothing is read back from the device.
+struct PackedShape {
+  int64_t batch;
+  int64_t total;  // points of all chains
+  int64_t max_points;
+};
+
+PackedShape check_packed(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Tensor& chain_points, int64_t max_points) {
+  check_cuda_float(lengths, "lengths");
+  check_like(angles, lengths, "angles");
+  check_like(dihedrals, lengths, "dihedrals");
+  TORCH_CHECK(lengths.dim() == 1 && angles.dim() == 1 && dihedrals.dim() == 1, "packed lengths, angles and dihedrals must be 1-D");
+  TORCH_CHECK(chain_points.is_cuda() && chain_points.device() == lengths.device(), "chain_points must be CUDA, on the device of lengths");
+  TORCH_CHECK(chain_points.scalar_type() == torch::kInt64 && chain_points.dim() == 1 && chain_points.is_contiguous(),
+              "chain_points must be a contiguous 1-D int64 tensor of B+1 offsets");
+  const int64_t batch = chain_points.size(0) - 1;
+  TORCH_CHECK(batch >= 0, "chain_points must hold B+1 offsets");
+  const int64_t total = lengths.size(0) + batch;
+  TORCH_CHECK(angles.size(0) == total - 2 * batch, "bad angles shape");
+  TORCH_CHECK(dihedrals.size(0) == total - 3 * batch, "bad dihedrals shape");
+  TORCH_CHECK(batch <= INT32_MAX, "shape exceeds int32 kernel limits");
+  TORCH_CHECK(batch == 0 || max_points >= 4, "point_count must be >= 4");
+  TORCH_CHECK(max_points - 3 <= kMaxSteps, "reconstruct supports at most ", kMaxSteps, " local transforms");
+  return {batch, total, max_points};
+}
+
+Tensor packed_forward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Tensor& chain_points,
+                           const PackedShape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor xyz = torch::empty({shape.total, 3}, lengths.options());
+  check_status(cufkb_block_forward_packed(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                          ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                          chain_points.data_ptr<int64_t>(), xyz.data_ptr(), shape.batch, shape.max_points, current_stream()),
+               "reconstruct_packed");
+  return xyz;
+}
+
+std::vector<Tensor> packed_backward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a,
+                                         const Tensor& chain_points, const Tensor& xyz, const Tensor& grad_points, const PackedShape& shape) {
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor gl = torch::empty_like(lengths);
+  Tensor ga = torch::empty_like(angles);
+  Tensor gd = torch::empty_like(dihedrals);
+  check_status(cufkb_block_backward_packed_from_xyz(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                                    ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                                    chain_points.data_ptr<int64_t>(), xyz.data_ptr(), grad_points.data_ptr(), gl.data_ptr(),
+                                                    ga.data_ptr(), gd.data_ptr(), shape.batch, shape.max_points, current_stream()),
+               "reconstruct_packed backward");
+  return {gl, ga, gd};
+}
+
+class PackedAutograd : public torch::autograd::Function<PackedAutograd> {
+ public:
+  static Tensor forward(AutogradContext* ctx, Tensor lengths, Tensor angles, Tensor dihedrals, Tensor chain_points, int64_t max_points,
+                       std::optional<Tensor> p0, std::optional<Tensor> first_direction, std::optional<Tensor> initial_normal) {
+    const PackedShape shape = check_packed(lengths, angles, dihedrals, chain_points, max_points);
+    const Anchors a{checked_anchor(opt(p0), lengths, "p0"), checked_anchor(opt(first_direction), lengths, "first_direction"),
+                    checked_anchor(opt(initial_normal), lengths, "initial_normal")};
+    Tensor xyz = packed_forward_impl(lengths, angles, dihedrals, a, chain_points, shape);
+    ctx->save_for_backward({lengths, angles, dihedrals, chain_points, xyz});
+    ctx->saved_data["max_points"] = max_points;
+    ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
+    ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
+    ctx->saved_data["initial_normal"] = a.initial_normal.defined() ? c10::IValue(a.initial_normal) : c10::IValue();
+    return xyz;
+  }
+
+  static tensor_list backward(AutogradContext* ctx, tensor_list grad_outputs) {
+    const auto saved = ctx->get_saved_variables();
+    Tensor grad_points = grad_outputs[0].is_contiguous() ? grad_outputs[0] : grad_outputs[0].contiguous();
+    check_like(grad_points, saved[0], "grad_points");
+    const PackedShape shape = check_packed(saved[0], saved[1], saved[2], saved[3], ctx->saved_data["max_points"].toInt());
+    auto anchor = [&](const char* key) {
+      const c10::IValue& v = ctx->saved_data[key];
+      return v.isTensor() ? v.toTensor() : Tensor();
+    };
+    const Anchors a{anchor("p0"), anchor("first_direction"), anchor("initial_normal")};
+    auto grads = packed_backward_impl(saved[0], saved[1], saved[2], a, saved[3], saved[4], grad_points, shape);
+    return {grads[0], grads[1], grads[2], Tensor(), Tensor(), Tensor(), Tensor(), Tensor()};
+  }
+};
+
+Tensor apply_packed(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Tensor& chain_points, int64_t max_points,
+                    const std::optional<Tensor>& p0, const std::optional<Tensor>& first_direction, const std::optional<Tensor>& initial_normal) {
+  return PackedAutograd::apply(lengths, angles, dihedrals, chain_points, max_points, p0, first_direction, initial_normal);
+}
+
 // ---------------------------------------------------------------------------------------------
 // torsion path: constants are a run-time argument (9 doubles), not a JIT build
 // ---------------------------------------------------------------------------------------------
@@ -423,6 +513,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("apply_long", &apply_long, "reconstruct autograd apply for chains of any length", pybind11::arg("lengths"), pybind11::arg("angles"),
         pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),
         pybind11::arg("initial_normal") = pybind11::none());
+  m.def("apply_packed", &apply_packed, "reconstruct autograd apply for a packed (ragged) batch", pybind11::arg("lengths"), pybind11::arg("angles"),
+        pybind11::arg("dihedrals"), pybind11::arg("chain_points"), pybind11::arg("max_points"), pybind11::arg("p0") = pybind11::none(),
+        pybind11::arg("first_direction") = pybind11::none(), pybind11::arg("initial_normal") = pybind11::none());
   m.def("torsion_apply", &torsion_apply, "torsion-only autograd apply", pybind11::arg("raw_pairs"), pybind11::arg("constants"));
   m.def("block_forward", &block_forward, "forward kernel only", pybind11::arg("lengths"), pybind11::arg("angles"),
         pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(), pybind11::arg("first_direction") = pybind11::none(),

@@ -86,3 +86,48 @@ def reconstruct_long(
     lengths, angles, dihedrals, single = _batched_inputs(lengths, angles, dihedrals)
     xyz = _C.apply_long(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
     return xyz[0] if single else xyz
+
+
+def reconstruct_packed(
+    lengths: torch.Tensor,
+    angles: torch.Tensor,
+    dihedrals: torch.Tensor,
+    chain_points: torch.Tensor,
+    p0: torch.Tensor | None = None,
+    first_direction: torch.Tensor | None = None,
+    initial_normal: torch.Tensor | None = None,
+    max_points: int | None = None,
+) -> torch.Tensor:
+    r"""``reconstruct`` for a packed (ragged) batch: chains of different lengths in one call.
+
+    The reference takes (B, N) batches only (block.cu:367-378).  Here chain b owns the points
+    ``[chain_points[b], chain_points[b+1])`` of the packed output, and its rows sit packed the same
+    way in the 1-D inputs: ``lengths`` has ``total - B`` entries (chain b's start at
+    ``chain_points[b] - b``), ``angles`` ``total - 2B`` (from ``chain_points[b] - 2b``) and
+    ``dihedrals`` ``total - 3B`` (from ``chain_points[b] - 3b``).
+
+    Args:
+        chain_points: ``(B + 1,)`` int64 offsets, ``chain_points[0] = 0``, nondecreasing, every chain
+            with 4 to 2051 points; on the device of ``lengths``.
+        max_points: the largest chain's point count.  When omitted it is read from
+            ``chain_points`` (one device-to-host copy, which also validates the offsets); pass it to
+            keep the call free of host synchronisation (then chains outside ``[4, max_points]`` are
+            skipped, their outputs left unset).
+
+    Returns:
+        ``(total, 3)`` packed coordinates, ``total = chain_points[-1]``.  Gradients flow to the packed
+        lengths, angles and dihedrals; anchors as in ``reconstruct``.
+    """
+    if max_points is None:
+        offsets = chain_points.detach().to("cpu", torch.int64)
+        counts = offsets[1:] - offsets[:-1]
+        if offsets.numel() < 1 or int(offsets[0]) != 0:
+            raise RuntimeError("chain_points must start at 0")
+        if counts.numel() and (int(counts.min()) < 4 or int(counts.max()) > BLOCK_SCAN_MAX_POINT_COUNT):
+            raise RuntimeError(f"every packed chain needs 4 to {BLOCK_SCAN_MAX_POINT_COUNT} points")
+        if int(offsets[-1]) != lengths.numel() + counts.numel():
+            raise RuntimeError("chain_points[-1] must equal the packed point count (lengths.numel() + B)")
+        max_points = int(counts.max()) if counts.numel() else 4
+    return _C.apply_packed(
+        lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), chain_points, int(max_points), p0, first_direction, initial_normal
+    )

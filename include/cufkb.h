@@ -107,6 +107,27 @@ CUFKB_API int cufkb_block_backward_from_xyz(int dtype, const void* lengths, cons
                                   void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
                                   cufkb_stream_t stream);
 
+/* Packed (ragged) batches: chains of different lengths in one call.  No counterpart in the
+ * reference, whose batches are (B, N) (src/cufk/csrc/block.cu:367-378).  chain_points is a device
+ * array of B+1 nondecreasing int64 offsets with chain_points[0] = 0: chain b has the points
+ * [chain_points[b], chain_points[b+1]) of the packed xyz (total_points, 3), and its rows sit packed
+ * the same way in lengths (total_points - B), angles (total_points - 2B) and dihedrals
+ * (total_points - 3B): chain b's lengths start at chain_points[b] - b, its angles at
+ * chain_points[b] - 2b, its dihedrals at chain_points[b] - 3b.  max_points is the largest chain
+ * (4 <= max_points <= 2051); the launch is planned for it.  A chain whose point count lies outside
+ * [4, max_points] is skipped: its outputs are left as they were.  The offsets stay on the device
+ * (nothing is read back), so these calls validate only what the host knows.  Anchors and dtypes as
+ * for the (B, N) entry points; the backward reads the forward's xyz as
+ * cufkb_block_backward_from_xyz does. */
+CUFKB_API int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                               const void* first_direction, const void* initial_normal, const int64_t* chain_points, void* xyz,
+                               int64_t batch, int64_t max_points, cufkb_stream_t stream);
+
+CUFKB_API int cufkb_block_backward_packed_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                         const void* first_direction, const void* initial_normal, const int64_t* chain_points,
+                                         const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
+                                         void* grad_dihedrals, int64_t batch, int64_t max_points, cufkb_stream_t stream);
+
 /* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
  * elements (any stride >= 0, pairs within a row contiguous). */
 CUFKB_API int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,

@@ -150,3 +150,23 @@ def test_status_strings(lib):
     assert b"2048 local transforms" in lib.cufkb_status_string(TOO_MANY_STEPS)
     assert lib.cufkb_status_string(12345) == b"unknown status"
     assert lib.cufkb_last_cuda_error() == 0
+
+
+def test_packed_entry_points_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_backward_packed_from_xyz.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+
+    def fwd_packed(offsets=128, batch=2, max_points=10, dtype=F32):
+        return lib.cufkb_block_forward_packed(dtype, 16, 32, 48, None, None, None, offsets, 64, batch, max_points, None)
+
+    assert fwd_packed(offsets=None) == NULL_POINTER
+    assert fwd_packed(offsets=132) == MISALIGNED  # int64 offsets need 8-byte alignment
+    assert fwd_packed(max_points=3) == POINT_COUNT
+    assert fwd_packed(max_points=2052) == TOO_MANY_STEPS
+    assert fwd_packed(dtype=7) == INVALID_DTYPE
+    assert fwd_packed(batch=0, offsets=None) == SUCCESS  # nothing to launch
+    bwd = lib.cufkb_block_backward_packed_from_xyz
+    assert bwd(F32, 16, 32, 48, None, None, None, None, 64, 80, 96, 112, 128, 2, 10, None) == NULL_POINTER
+    assert bwd(F32, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 2, 2052, None) == TOO_MANY_STEPS
+    assert bwd(F16, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 0, 10, None) == SUCCESS
