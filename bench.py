@@ -46,6 +46,22 @@ L2_BYTES = 126 * 1024 * 1024
 HBM_FALLBACK_GBS = 6650.0
 
 
+# The other configurations of the path (one JSON line each, not the headline): kind, chains,
+# points, dtype, anchors.
+WORKLOADS = {
+    "cfg2-f32": ("block", 2048, 2051, torch.float32, True),
+    "cfg2-f64": ("block", 2048, 2051, torch.float64, True),
+    "cfg3-f32": ("torsion", 16384, 768, torch.float32, False),
+    "cfg3-bf16": ("torsion", 16384, 768, torch.bfloat16, False),
+    "cfg4-f16": ("block", 8192, 1026, torch.float16, False),
+    "cfg4-bf16": ("block", 8192, 1026, torch.bfloat16, False),
+    # the fused consumer (reconstruct_mse) on the config-1 shape, beside the unfused sequence
+    "mse-cfg1": ("mse", 4096, 768, torch.float32, False),
+}
+BACKBONE_LENGTHS = (0.14685231, 0.15365194, 0.13405086)
+BACKBONE_ANGLES = (1.9676635, 2.062335, 2.164016)
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -56,6 +72,12 @@ def parse_args(argv=None):
     ap.add_argument("--points", type=int, default=POINTS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument(
+        "--workload",
+        choices=["cfg1", *WORKLOADS],
+        default="cfg1",
+        help="cfg1 (default) is the headline line; the others time the remaining configurations of the path",
+    )
     return ap.parse_args(argv)
 
 
@@ -519,6 +541,179 @@ def cpu_baseline(points: int, budget_s: float = 12.0, chains: int = 256) -> dict
     }
 
 
+def workload_inputs(kind: str, batch: int, points: int, dtype, anchors: bool, seed: int) -> dict:
+    """Seeded synthetic inputs of one configuration, generated in float64 on the CPU then cast:
+    block rows as in ``make_inputs`` (anchors: p0 ~ N(0,1)^3, first_direction / initial_normal a
+    random orthonormal pair); torsion raw pairs (B, 2(N-3)) ~ N(0,1); grad_out ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    f64 = torch.float64
+    out = {}
+    if kind in ("block", "mse"):
+        base = make_inputs(batch, points, seed=seed)
+        out = {k: base[k].to(f64).to(dtype) for k in ("lengths", "angles", "dihedrals", "grad")}
+        if kind == "mse":
+            # a target: the grad tensor's shape, values of the coordinate scale
+            out["target"] = (3.0 * out.pop("grad").to(f64)).to(dtype)
+        if anchors:
+            q, _ = torch.linalg.qr(torch.randn(3, 3, generator=g, dtype=f64))
+            out["p0"] = torch.randn(3, generator=g, dtype=f64).to(dtype)
+            out["first_direction"] = q[:, 0].contiguous().to(dtype)
+            out["initial_normal"] = q[:, 1].contiguous().to(dtype)
+    else:
+        out["raw"] = torch.randn(batch, 2 * (points - 3), generator=g, dtype=f64).to(dtype)
+        out["grad"] = torch.randn(batch, points, 3, generator=g, dtype=f64).to(dtype)
+    return out
+
+
+def run_workload(args, dist: Dist) -> dict:
+    """One configuration other than the headline: forward + backward (the kernels autograd runs)
+    on this rank's shard, CUDA graphs over rotating input sets, per-kernel launch times and
+    algorithmic-byte rooflines."""
+    sys.path.insert(0, str(ROOT))
+    import cufk_b200  # noqa: F401
+    from cufk_b200 import _native
+    from cufk_b200.torsion import torsion_constants
+
+    C = _native._C
+    kind, batch, points, dtype, anchors = WORKLOADS[args.workload]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lo, hi = shard(batch, dist.world, dist.rank)
+    host = workload_inputs(kind, batch, points, dtype, anchors, seed=0)
+    host = {k: (v[lo:hi].contiguous() if v.dim() > 1 else v) for k, v in host.items()}
+    elem = torch.empty(0, dtype=dtype).element_size()
+    b_local = hi - lo
+    steps_s = points - 3
+    if kind == "block":
+        fwd_b, bwd_b = (6 * points - 6) * elem, (9 * points - 12) * elem
+        names = ("block_forward_kernel", "block_backward_xyz_kernel" if elem >= 4 else "block_backward_kernel")
+    elif kind == "mse":
+        # one kernel: read lengths/angles/dihedrals and the target, write the three gradient rows
+        fwd_b, bwd_b = (9 * points - 12) * elem, 0
+        names = ("block_mse_kernel", None)
+    else:
+        fwd_b, bwd_b = (2 * steps_s + 3 * points) * elem, (4 * steps_s + 3 * points) * elem
+        names = ("torsion_forward_kernel", "torsion_backward_xyz_kernel" if elem >= 4 else "torsion_backward_kernel")
+    set_bytes = b_local * (fwd_b + bwd_b)
+    n_sets = max(2, min(16, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
+    consts = torsion_constants(BACKBONE_LENGTHS, BACKBONE_ANGLES)
+    sets = []
+    for i in range(n_sets):
+        d = {k: v.to(dev) for k, v in host.items()}
+        if kind in ("block", "mse"):
+            d["dihedrals"] = d["dihedrals"] + 1e-3 * i
+        else:
+            d["raw"] = d["raw"] + 1e-3 * i
+        sets.append(d)
+    anchor_args = lambda d: (d.get("p0"), d.get("first_direction"), d.get("initial_normal"))  # noqa: E731
+
+    def unfused(d):
+        # the sequence the fused kernel replaces: forward, the loss and dL/dxyz in torch, backward
+        xyz = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+        diff = xyz - d["target"]
+        d["loss_unfused"] = (diff * diff).sum(-1).mean(-1)
+        return C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, diff * (2.0 / points))
+
+    def fwd(d):
+        if kind == "mse":
+            return C.block_mse(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["target"], True)
+        if kind == "block":
+            return C.block_forward(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d))
+        return C.torsion_forward(d["raw"], consts)
+
+    def bwd(d, xyz):
+        if kind == "block":
+            return C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d), xyz, d["grad"])
+        return C.torsion_backward_from_xyz(d["raw"], consts, xyz, d["grad"])
+
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    g_step, g_fwd, g_bwd, g_unfused = [], [], [], []
+    with torch.cuda.stream(stream):
+        for d in sets:
+            d["xyz"] = fwd(d)
+            if kind == "mse":
+                unfused(d)
+            else:
+                bwd(d, d["xyz"])
+        stream.synchronize()
+        for d in sets:
+            if kind == "mse":
+                bodies = ((g_step, lambda d=d: fwd(d)), (g_unfused, lambda d=d: unfused(d)))
+            else:
+                bodies = ((g_step, lambda d=d: bwd(d, fwd(d))), (g_fwd, lambda d=d: fwd(d)), (g_bwd, lambda d=d: bwd(d, d["xyz"])))
+            for lst, body in bodies:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    body()
+                lst.append(gr)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index)
+    extra = {}
+    with torch.cuda.stream(stream):
+        with sampler:
+            ms_total = time_graphs(g_step, args.steps, args.warmup, dist, stream)
+        if kind == "mse":
+            ms_fwd, ms_bwd = ms_total / args.steps, 0.0
+            ms_unfused = time_graphs(g_unfused, args.steps, args.warmup, dist, stream) / args.steps
+            extra["unfused"] = {
+                "ms_per_step": ms_unfused,
+                "value": batch * points / (ms_unfused * 1e-3),
+                "sequence": "block_forward_kernel, torch loss and dL/dxyz (3 elementwise/reduction kernels), block_backward_xyz_kernel",
+            }
+        else:
+            ms_fwd = time_graphs(g_fwd, args.steps, args.warmup, dist, stream) / args.steps
+            ms_bwd = time_graphs(g_bwd, args.steps, args.warmup, dist, stream) / args.steps
+    ms_step = ms_total / args.steps
+    peak, peak_kind = measured_peak()
+    per_kernel = {}
+    for name, ms, nbytes in ((names[0], ms_fwd, fwd_b), (names[1], ms_bwd, bwd_b)):
+        if name is None:
+            continue
+        gbs = nbytes * b_local / (ms * 1e-3) / 1e9
+        per_kernel[name] = {"launch_ms": round(ms, 5), "bytes_per_atom": round(nbytes / points, 3), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["launch_ms"])
+    return {
+        "metric": f"fwd+bwd atoms/s ({args.workload}: {kind}, B={batch}, N={points}, {str(dtype).replace('torch.', '')})",
+        "value": batch * points / (ms_step * 1e-3),
+        "unit": "atoms/s",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": {torch.float32: "f32", torch.float64: "f64", torch.float16: "f16", torch.bfloat16: "bf16"}[dtype],
+        "data": "synthetic (seeded, the distributions of the configuration)",
+        "config": {
+            "workload": args.workload,
+            "kind": kind,
+            "global_batch": batch,
+            "points": points,
+            "anchors": anchors,
+            "per_gpu_batch": b_local,
+            "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB",
+            "timing": "one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks",
+        },
+        "roofline": {
+            "kernel": dom,
+            "bound": "hbm",
+            "achieved": per_kernel[dom]["achieved_gbs"],
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": per_kernel[dom]["frac"],
+            "peak_source": peak_kind,
+            "traffic": None,
+            "per_kernel": per_kernel,
+            "step_frac": round((fwd_b + bwd_b) * b_local / (ms_step * 1e-3) / 1e9 / peak, 4),
+        },
+        "gpu_launches": (1 if names[1] is None else 2) * args.steps,
+        "kernels": names[0] if names[1] is None else f"{names[0]} + {names[1]} per step",
+        "clocks": sampler.summary(),
+        **extra,
+    }
+
+
 def run_reference(args) -> dict | None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -574,7 +769,7 @@ def main(argv=None) -> int:
         return 0
     dist = Dist(args.gpus)
     try:
-        out = run_ours(args, dist)
+        out = run_ours(args, dist) if args.workload == "cfg1" else run_workload(args, dist)
     finally:
         torch.cuda.synchronize()
         dist.close()

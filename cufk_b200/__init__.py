@@ -4,11 +4,13 @@
 ``reconstruct``, ``compile_torsion``, ``BLOCK_SCAN_MAX_POINT_COUNT`` and ``__version__``; and
 ``reconstruct_long`` for chains longer than ``BLOCK_SCAN_MAX_POINT_COUNT``, which the reference
 does not support; ``reconstruct_packed`` for ragged batches (chains of different lengths, packed);
+``reconstruct_mse``, the reconstruction fused with a coordinate loss and its gradient;
 and ``ops``, the same path as ``torch.library`` operators
 (``torch.ops.cufk_b200.*``) that ``torch.compile`` traces through.
 """
 
 from .reconstruct import BLOCK_SCAN_MAX_POINT_COUNT, reconstruct, reconstruct_long, reconstruct_packed
+from .losses import reconstruct_mse
 from .torsion import compile_torsion
 from . import ops  # noqa: E402  (registers the torch.library operators)
 
@@ -21,5 +23,6 @@ __all__ = [
     "ops",
     "reconstruct",
     "reconstruct_long",
+    "reconstruct_mse",
     "reconstruct_packed",
 ]

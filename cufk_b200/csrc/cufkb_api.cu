@@ -21,7 +21,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 40;
+constexpr int kNumKernels = 44;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -239,7 +239,8 @@ enum KernelKind {
   kLongTotals = 6,
   kLongForward = 7,
   kLongSums = 8,
-  kLongBackward = 9
+  kLongBackward = 9,
+  kBlockMse = 10
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
@@ -288,6 +289,24 @@ int block_backward_xyz_impl(const void* L, const void* A, const void* D, const v
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Fused consumer: reconstruction, mean squared distance to a target, and (grads non-null) its
+// gradient with respect to the parameters, in one kernel (32- and 64-bit types).
+template <typename T>
+int block_mse_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* target, void* loss, void* gL,
+                   void* gA, void* gD, int64_t batch, int points, cudaStream_t stream) {
+  const size_t smem = cufkb::block_smem_bytes<T>(points, true);
+  auto kernel = cufkb::block_mse_kernel<T>;
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockMse, dtype_index<T>()), batch, points, smem, kXyzTargetWarpsPerSm)) return st;
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(target), static_cast<T*>(loss), static_cast<T*>(gL),
                                                                           static_cast<T*>(gA), static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
@@ -582,6 +601,29 @@ int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* an
                                           grad_angles, grad_dihedrals, batch, points, stream);
 }
 
+int cufkb_block_mse(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                    const void* initial_normal, const void* target, void* loss, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                    int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch == 0) return CUFKB_SUCCESS;
+  const bool grads = grad_lengths || grad_angles || grad_dihedrals;
+  if (grads && !(grad_lengths && grad_angles && grad_dihedrals)) return CUFKB_ERROR_NULL_POINTER;
+  if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, target, loss},
+                                    {lengths, angles, dihedrals, p0, first_direction, initial_normal, target, loss, grad_lengths, grad_angles,
+                                     grad_dihedrals})) {
+    return st;
+  }
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT32) {
+    return block_mse_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, target, loss, grad_lengths, grad_angles, grad_dihedrals,
+                                 batch, n, s);
+  }
+  return block_mse_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, target, loss, grad_lengths, grad_angles, grad_dihedrals,
+                                batch, n, s);
+}
+
 int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                                const void* initial_normal, const int64_t* chain_points, void* xyz, int64_t batch, int64_t max_points,
                                cufkb_stream_t stream) {
@@ -767,7 +809,7 @@ const char* cufkb_status_string(int status) {
     case CUFKB_ERROR_WORKSPACE:
       return "workspace is smaller than cufkb_block_long_workspace_bytes";
     case CUFKB_ERROR_UNSUPPORTED_DTYPE:
-      return "chains longer than 2051 points support float32 and float64";
+      return "this path supports float32 and float64 only (chains longer than 2051 points, the fused loss)";
     case CUFKB_ERROR_SCRATCH_CAPACITY:
       return "batch x segments exceeds the 2 MiB static scratch of cufkb_block_forward_long_static";
     default:

@@ -611,59 +611,18 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockA
   write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, tid, nthr);
 }
 
-// Backward from the forward's xyz (4- and 8-byte types, base frame orthonormal).  In world
-// coordinates every gradient of step s needs only the positions around it and the suffix sums
-// F_s = sum_{j >= s+3} g_j, M_s = sum_{j >= s+3} (x_j - o) x g_j (moments about the chain's own
-// p2 = o, so that tau keeps its precision however far the chain is from the world origin):
-//   u_b = (x_{b+1} - x_b) / |x_{b+1} - x_b|          (bond b; u_{s+1} = P_{s-1}.col0, u_{s+2} = P_s.col0)
-//   P_s.col2 = (u_{s+1} x u_{s+2}) / sin(theta_s)    (the frame normal; |u_{s+1} x u_{s+2}| = sin theta_s)
-// so no local transform is rebuilt: the chain's xyz and grad rows are staged (16-byte LDGSTS), each
-// thread sums g and (x - o) x g over its atoms, an exclusive suffix scan gives the sums of all later
-// threads, and one sweep up the thread's steps produces the three gradients, written over the
-// grad row in place (step s only reads g_{s+3}, its own atom).  A chain is redone by the recompute
-// form in the same CTA when its base frame is not orthonormal, when a bond is shorter than
-// 1e-3 |x|max (its direction from rounded positions would be off by more than ~1e-4: a zero-length
-// bond, or a chain far from the origin relative to its bond lengths), when a plane normal has
-// sin^2 theta < 1e-2 (bond angle within ~6 degrees of 0 or pi), or when a value is not finite.
-template <typename T>
-__global__ void __launch_bounds__(kMaxWarps* kWarp)
-    block_backward_xyz_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
-                              T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
-  using R = typename ComputeOf<T>::type;
-  using V = R;
-  static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ CtaExchange<V> ex;
-
-  const int64_t chain = blockIdx.x;
-  const ChainRows rows = chain_rows(geo, chain);
-  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
-  const int N = rows.points, St = N - 3, K = geo.items;
-  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
-  const T* grow = grad_xyz + rows.xyz;
-  unsigned char* const slot_region = smem;
-  unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
-  ChainViews<T> cv;
-  cv.Y = stage_row_async(slot_region, xyz + rows.xyz, 3 * N, tid, nthr);
-  cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
-  cv.X = cv.G;  // gradients go over the consumed grad row
-  // thread 0 classifies the base frame while the rows stage; the first frame itself is only needed
-  // again by thread 0 for the first-frame gradients (and by the recompute form)
-  auto first_frame = [&]() {
-    const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
-    const R l0 = to_r<R>(args.lengths[rows.lengths]);
-    const R l1 = to_r<R>(args.lengths[rows.lengths + 1]);
-    const R a0 = to_r<R>(args.angles[rows.angles]);
-    return FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
-  };
-  // thread 0 builds the first frame while the rows stage and keeps it in shared memory for the
-  // first-frame gradients at the end (no dependent global loads on the CTA's critical path there)
-  __shared__ FirstFrame<V> first;
-  if (tid == 0) first = first_frame();
-  const StepRange range = step_range(tid, K, St);
-  cp_async_wait_all();
-  __syncthreads();
-
+// The xyz-form backward of one chain whose xyz (cv.Y) and grad row (cv.G) are staged in shared
+// memory (slot_region and grad_region), with its first frame in `first`.  Leaves the three
+// gradients in the slots cv.X points at: the grad row, or the slot region when the chain takes the
+// recompute form.  restore_grad() puts the grad row back in shared memory for that form (the
+// sweep may have written gradients over part of it before the chain was found degenerate): a
+// restaging of the global row, or (fused consumer) a recomputation; the redo path waits for its
+// copies and synchronises after it.
+template <typename T, typename V, typename RestoreGrad>
+__device__ __forceinline__ void backward_xyz_staged(ChainViews<T>& cv, CtaExchange<V>& ex, const FirstFrame<V>& first, const BlockArgs<T>& args,
+                                                    const ChainRows& rows, unsigned char* slot_region, StepRange range, int nwarps,
+                                                    RestoreGrad restore_grad) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
   const bool general = first.bf.general;  // uniform over the CTA
   bool redo = general;
   if (!redo) {
@@ -764,10 +723,11 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   if (redo) {
     const AnchorFrame<V>& af = first.af;
     const BackwardFrame<V>& bf = first.bf;
-    // recompute form, laid out as in block_backward_kernel: inputs into the slots, grad row restaged
+    // recompute form, laid out as in block_backward_kernel: the grad row restored (the sweep may
+    // have written gradients over part of it), then the inputs into the slots
     __syncthreads();
+    restore_grad();
     stage_block_inputs<T>(cv, slot_region, args, rows, 0, tid, nthr);
-    cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
     cp_async_wait_all();
     __syncthreads();
     auto step = [&](int s) {
@@ -777,11 +737,168 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
       return step_rot(l, st, ct, sp, cp);
     };
     if (general) {
-      block_backward_general<T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+      block_backward_general<T, V>(cv, ex, af, bf, cv.G, range, nwarps, step);
     } else {
-      block_backward_recompute<true, T, V>(cv, ex, af, bf, grow, range, nwarps, step);
+      block_backward_recompute<true, T, V>(cv, ex, af, bf, cv.G, range, nwarps, step);
     }
   }
+}
+
+// Backward from the forward's xyz (4- and 8-byte types, base frame orthonormal).  In world
+// coordinates every gradient of step s needs only the positions around it and the suffix sums
+// F_s = sum_{j >= s+3} g_j, M_s = sum_{j >= s+3} (x_j - o) x g_j (moments about the chain's own
+// p2 = o, so that tau keeps its precision however far the chain is from the world origin):
+//   u_b = (x_{b+1} - x_b) / |x_{b+1} - x_b|          (bond b; u_{s+1} = P_{s-1}.col0, u_{s+2} = P_s.col0)
+//   P_s.col2 = (u_{s+1} x u_{s+2}) / sin(theta_s)    (the frame normal; |u_{s+1} x u_{s+2}| = sin theta_s)
+// so no local transform is rebuilt: the chain's xyz and grad rows are staged (16-byte LDGSTS), each
+// thread sums g and (x - o) x g over its atoms, an exclusive suffix scan gives the sums of all later
+// threads, and one sweep up the thread's steps produces the three gradients, written over the
+// grad row in place (step s only reads g_{s+3}, its own atom).  A chain is redone by the recompute
+// form in the same CTA when its base frame is not orthonormal, when a bond is shorter than
+// 1e-3 |x|max (its direction from rounded positions would be off by more than ~1e-4: a zero-length
+// bond, or a chain far from the origin relative to its bond lengths), when a plane normal has
+// sin^2 theta < 1e-2 (bond angle within ~6 degrees of 0 or pi), or when a value is not finite.
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    block_backward_xyz_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
+                              T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+
+  const int64_t chain = blockIdx.x;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, St = N - 3, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  const T* grow = grad_xyz + rows.xyz;
+  unsigned char* const slot_region = smem;
+  unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
+  ChainViews<T> cv;
+  cv.Y = stage_row_async(slot_region, xyz + rows.xyz, 3 * N, tid, nthr);
+  cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
+  cv.X = cv.G;  // gradients go over the consumed grad row
+  // thread 0 classifies the base frame while the rows stage; the first frame itself is only needed
+  // again by thread 0 for the first-frame gradients (and by the recompute form)
+  auto first_frame = [&]() {
+    const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+    const R l0 = to_r<R>(args.lengths[rows.lengths]);
+    const R l1 = to_r<R>(args.lengths[rows.lengths + 1]);
+    const R a0 = to_r<R>(args.angles[rows.angles]);
+    return FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
+  };
+  // thread 0 builds the first frame while the rows stage and keeps it in shared memory for the
+  // first-frame gradients at the end (no dependent global loads on the CTA's critical path there)
+  __shared__ FirstFrame<V> first;
+  if (tid == 0) first = first_frame();
+  const StepRange range = step_range(tid, K, St);
+  cp_async_wait_all();
+  __syncthreads();
+
+  auto restore_grad = [&]() { cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr); };
+  backward_xyz_staged<T, V>(cv, ex, first, args, rows, slot_region, range, nwarps, restore_grad);
+  __syncthreads();
+  write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, tid, nthr);
+}
+
+// --------------------------------------------------------------------------------------------
+// fused consumer: reconstruction, a coordinate loss and its backward in one CTA per chain
+// --------------------------------------------------------------------------------------------
+// loss[b] = (1/N) sum_j |x_j - t_j|^2 for the chain's xyz x (as block_forward_kernel builds it) and a
+// target row t, and, when grad_lengths is not null, d loss[b] / d (lengths, angles, dihedrals) of
+// the chain.  The chain never leaves shared memory: its inputs are staged into the slots and the
+// target row into the grad region, the forward leaves x in the slots, one pass forms the loss and
+// dL/dx = (2/N)(x - t) over the target row, and the xyz-form backward (backward_xyz_staged) turns
+// that into the parameter gradients.  HBM traffic per atom (float32): 12 B of inputs + 12 B of
+// target + 12 B of gradients, where the unfused chain (forward, a separate loss, backward) moves the
+// xyz out and back in between.
+template <typename T>
+__global__ void __launch_bounds__(kMaxWarps* kWarp)
+    block_mse_kernel(BlockArgs<T> args, const T* __restrict__ target, T* __restrict__ loss, T* __restrict__ grad_lengths, T* __restrict__ grad_angles,
+                     T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  using R = typename ComputeOf<T>::type;
+  using V = R;
+  static_assert(sizeof(T) >= 4, "the fused consumer serves 32- and 64-bit types");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ CtaExchange<V> ex;
+  __shared__ FirstFrame<V> first;
+
+  const int64_t chain = blockIdx.x;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, St = N - 3, K = geo.items;
+  const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
+  unsigned char* const slot_region = smem;
+  unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
+  const T* trow = target + rows.xyz;
+  ChainViews<T> cv;
+  stage_block_inputs<T>(cv, slot_region, args, rows, 0, tid, nthr);
+  cv.G = stage_row_async(grad_region, trow, 3 * N, tid, nthr);
+  if (tid == 0) {
+    // the first frame from global memory while the rows stage (as the xyz backward builds it)
+    const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
+    const R l0 = to_r<R>(args.lengths[rows.lengths]);
+    const R l1 = to_r<R>(args.lengths[rows.lengths + 1]);
+    const R a0 = to_r<R>(args.angles[rows.angles]);
+    first = FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // forward: the operations of block_forward_kernel, xyz left in the slots
+  const ChainFrame<V>& ff = first.bf.ff;
+  if (tid == 0) {
+    // atoms 0..2; their slots held lengths[0..1] and angles[0], which no step reads
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      cv.set_slot(i, first.af.p0[i]);
+      cv.set_slot(3 + i, ff.p1[i]);
+      cv.set_slot(6 + i, ff.p2[i]);
+    }
+  }
+  auto step = [&](int s) {
+    V l, th, ph, st, ct, sp, cp;
+    block_step_inputs<T>(cv, s, l, th, ph);
+    step_sincos(th, ph, st, ct, sp, cp);
+    return step_rot(l, st, ct, sp, cp);
+  };
+  const StepRange range = step_range(tid, K, St);
+  const Affine<V> total = sweep_local_prefix<T, V>(cv, range, step);
+  const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), ff.F, ff.p2);
+  apply_carry<T, V>(cv, W, range);
+  __syncthreads();
+
+  // loss and dL/dx = (2/N)(x - t) over the target row
+  const V inv_n = V(1) / V(N);
+  const V two_inv_n = V(2) * inv_n;
+  auto make_grad = [&]() {
+    V part = V(0);
+    for (int e = tid; e < 3 * N; e += nthr) {
+      const V d = vsub(cv.slot(e), to_r<V>(cv.G[e]));
+      part = vfma(d, d, part);
+      cv.G[e] = from_r<T>(vmul(two_inv_n, d));
+    }
+    return part;
+  };
+  const V sum = cta_sum_to_thread0<V>(make_grad(), ex.warp_red, nwarps);
+  if (tid == 0) loss[chain] = from_r<T>(vmul(sum, inv_n));
+  if (grad_lengths == nullptr) return;  // uniform over the CTA: the loss alone
+  __syncthreads();
+
+  // backward from x (in the slots) and dL/dx (over the target row)
+  cv.Y = reinterpret_cast<const T*>(cv.X);
+  cv.X = cv.G;
+  auto restore_grad = [&]() {
+    // the target again, and dL/dx from the positions, which are still in the slots
+    stage_row_async(grad_region, trow, 3 * N, tid, nthr);
+    cp_async_wait_all();
+    __syncthreads();
+    for (int e = tid; e < 3 * N; e += nthr) cv.G[e] = from_r<T>(vmul(two_inv_n, vsub(cv.pos(e), to_r<V>(cv.G[e]))));
+    __syncthreads();
+  };
+  backward_xyz_staged<T, V>(cv, ex, first, args, rows, slot_region, range, nwarps, restore_grad);
   __syncthreads();
   write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, tid, nthr);
 }

@@ -126,6 +126,7 @@ void check_status(int status, const char* op) {
 }
 
 const void* ptr_or_null(const Tensor& t) { return t.defined() ? t.data_ptr() : nullptr; }
+void* out_ptr_or_null(const Tensor& t) { return t.defined() ? t.data_ptr() : nullptr; }
 
 cufkb_stream_t current_stream() { return reinterpret_cast<cufkb_stream_t>(at::cuda::getCurrentCUDAStream().stream()); }
 
@@ -486,6 +487,30 @@ std::vector<Tensor> block_backward_from_xyz(const Tensor& lengths, const Tensor&
   return block_backward_xyz_impl(lengths, angles, dihedrals, a, xyz, grad_points, shape);
 }
 
+// Fused consumer (cufkb_block_mse): per-chain mean squared distance of the reconstruction to a
+// target and, with_grads, its gradient with respect to lengths, angles and dihedrals.
+std::vector<Tensor> block_mse(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                              const std::optional<Tensor>& fd, const std::optional<Tensor>& nn, const Tensor& target, bool with_grads) {
+  const Shape shape = check_geom(lengths, angles, dihedrals);
+  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
+  TORCH_CHECK(lengths.scalar_type() == torch::kFloat32 || lengths.scalar_type() == torch::kFloat64, "reconstruct_mse supports float32 and float64");
+  check_like(target, lengths, "target");
+  TORCH_CHECK(target.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "target must have shape (B, N, 3)");
+  const c10::cuda::CUDAGuard guard(lengths.device());
+  Tensor loss = torch::empty({shape.batch}, lengths.options());
+  Tensor gl, ga, gd;
+  if (with_grads) {
+    gl = torch::empty_like(lengths);
+    ga = torch::empty_like(angles);
+    gd = torch::empty_like(dihedrals);
+  }
+  check_status(cufkb_block_mse(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(), ptr_or_null(a.p0),
+                               ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), target.data_ptr(), loss.data_ptr(), out_ptr_or_null(gl),
+                               out_ptr_or_null(ga), out_ptr_or_null(gd), shape.batch, shape.points, current_stream()),
+               "reconstruct_mse");
+  return {loss, gl, ga, gd};
+}
+
 Tensor torsion_forward(const Tensor& raw, const std::vector<double>& consts) { return torsion_forward_impl(raw, consts, check_pairs(raw)); }
 
 Tensor torsion_backward(const Tensor& raw, const std::vector<double>& consts, const Tensor& grad_points) {
@@ -526,6 +551,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("block_backward_from_xyz", &block_backward_from_xyz, "backward kernel reading the forward's xyz", pybind11::arg("lengths"),
         pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
         pybind11::arg("xyz"), pybind11::arg("grad_points"));
+  m.def("block_mse", &block_mse, "fused reconstruction + mean squared distance to a target (+ gradients)", pybind11::arg("lengths"),
+        pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
+        pybind11::arg("target"), pybind11::arg("with_grads"));
   m.def("torsion_forward", &torsion_forward, "torsion forward kernel only");
   m.def("torsion_backward", &torsion_backward, "torsion backward kernel only");
   m.def("torsion_backward_from_xyz", &torsion_backward_from_xyz, "torsion backward kernel reading the forward's xyz");

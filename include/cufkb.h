@@ -67,7 +67,7 @@ enum cufkb_status {
   CUFKB_ERROR_INVALID_VALUE = 8,  /* NULL torsion constants */
   CUFKB_ERROR_CUDA = 9,           /* a CUDA runtime error; see cufkb_last_cuda_error() */
   CUFKB_ERROR_WORKSPACE = 10,     /* workspace smaller than cufkb_block_long_workspace_bytes */
-  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11, /* the long-chain path: float32 and float64 only */
+  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11, /* the long-chain path and the fused loss: float32 and float64 only */
   CUFKB_ERROR_SCRATCH_CAPACITY = 12   /* cufkb_block_forward_long_static: call too large for its scratch */
 };
 
@@ -106,6 +106,17 @@ CUFKB_API int cufkb_block_backward_from_xyz(int dtype, const void* lengths, cons
                                   const void* first_direction, const void* initial_normal, const void* xyz, const void* grad_xyz,
                                   void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
                                   cufkb_stream_t stream);
+
+/* Fused consumer: loss[b] = (1/N) sum_j |xyz_j - target_j|^2 for each chain's reconstruction
+ * (as cufkb_block_forward builds it, with the same arguments) and a target (B, N, 3), and, unless
+ * grad_lengths, grad_angles and grad_dihedrals are all NULL, d loss[b] / d (lengths, angles,
+ * dihedrals) of each chain.  One kernel: the chain's xyz stays in shared memory, so neither xyz nor
+ * d loss / d xyz is written to device memory.  loss is (B,).  float32 and float64 only
+ * (CUFKB_ERROR_UNSUPPORTED_DTYPE otherwise).  No counterpart in the reference, whose path ends at
+ * xyz. */
+CUFKB_API int cufkb_block_mse(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                    const void* first_direction, const void* initial_normal, const void* target, void* loss, void* grad_lengths,
+                    void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream);
 
 /* Packed (ragged) batches: chains of different lengths in one call.  No counterpart in the
  * reference, whose batches are (B, N) (src/cufk/csrc/block.cu:367-378).  chain_points is a device

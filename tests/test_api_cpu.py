@@ -17,7 +17,7 @@ PKG = Path(cufk.__file__).resolve().parent
 def test_public_surface_matches_reference():
     # the reference's surface, plus reconstruct_long for chains the reference cannot reconstruct and
     # ops, the same path as torch.library operators
-    assert set(cufk.__all__) == {"BLOCK_SCAN_MAX_POINT_COUNT", "__version__", "compile_torsion", "ops", "reconstruct", "reconstruct_long", "reconstruct_packed"}
+    assert set(cufk.__all__) == {"BLOCK_SCAN_MAX_POINT_COUNT", "__version__", "compile_torsion", "ops", "reconstruct", "reconstruct_long", "reconstruct_mse", "reconstruct_packed"}
     assert cufk.BLOCK_SCAN_MAX_POINT_COUNT == 2051
     assert cufk.__version__ == "0.1.0"
 

@@ -170,3 +170,14 @@ def test_packed_entry_points_validation(lib):
     assert bwd(F32, 16, 32, 48, None, None, None, None, 64, 80, 96, 112, 128, 2, 10, None) == NULL_POINTER
     assert bwd(F32, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 2, 2052, None) == TOO_MANY_STEPS
     assert bwd(F16, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 0, 10, None) == SUCCESS
+
+
+def test_fused_mse_entry_point_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_mse.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    mse = lib.cufkb_block_mse
+    assert mse(F16, 16, 32, 48, None, None, None, 64, 80, None, None, None, 2, 10, None) == 11  # float32/float64 only
+    assert mse(F32, 16, 32, 48, None, None, None, 64, 80, 96, None, None, 2, 10, None) == NULL_POINTER  # all three grads or none
+    assert mse(F32, 16, 32, 48, None, None, None, None, 80, None, None, None, 2, 10, None) == NULL_POINTER  # target required
+    assert mse(F32, 16, 32, 48, None, None, None, 64, 80, None, None, None, 2, 3, None) == POINT_COUNT
+    assert mse(F64, 16, 32, 48, None, None, None, 64, 80, None, None, None, 0, 10, None) == SUCCESS

@@ -1,0 +1,126 @@
+"""The fused consumer (reconstruct_mse: reconstruction + mean squared distance to a target + its
+gradient, one kernel) on the GPU, against float64 autograd through the oracle forward and against
+the unfused sequence (reconstruct, a torch loss, backward), including chains that take the
+recompute form inside the fused kernel."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+import cufk_b200 as cufk
+from oracle import nerf64
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+F64 = torch.float64
+KEYS = ("p0", "first_direction", "initial_normal")
+
+
+def oracle_mse(inp, target, anchors):
+    L, A, D = (inp[k].detach().to(F64).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    kw = {k: inp[k].to(F64) for k in KEYS} if anchors else {}
+    xyz = nerf64.reconstruct64(L, A, D, **kw)
+    loss = ((xyz - target.to(F64)) ** 2).sum(-1).mean(-1)
+    gl, ga, gd = torch.autograd.grad(loss.sum(), (L, A, D))
+    return loss.detach(), gl, ga, gd
+
+
+def fused(inp, target, dtype, anchors, grad_loss=None):
+    L, A, D = (inp[k].to(DEV, dtype).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    kw = {k: inp[k].to(DEV, dtype) for k in KEYS} if anchors else {}
+    loss = cufk.reconstruct_mse(L, A, D, target.to(DEV, dtype), **kw)
+    loss.backward(torch.ones_like(loss) if grad_loss is None else grad_loss.to(DEV, dtype))
+    return loss.detach().cpu(), L.grad.cpu(), A.grad.cpu(), D.grad.cpu()
+
+
+def rel(a, b):
+    return float((a.double() - b).norm() / b.norm().clamp_min(1e-300))
+
+
+def target_for(inp, anchors, seed):
+    """A target near the chain: its float64 reconstruction plus noise."""
+    kw = {k: inp[k].to(F64) for k in KEYS} if anchors else {}
+    xyz = nerf64.reconstruct64(inp["lengths"], inp["angles"], inp["dihedrals"], **kw)
+    g = torch.Generator().manual_seed(seed)
+    return xyz + 0.3 * torch.randn(xyz.shape, generator=g, dtype=F64)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, F64])
+@pytest.mark.parametrize("points,anchors", [(4, False), (37, True), (768, False), (2051, True)])
+def test_fused_loss_matches_float64(dtype, points, anchors):
+    inp = nerf64.make_inputs(9, points, seed=points, anchors=anchors)
+    target = target_for(inp, anchors, seed=points + 1)
+    got = fused(inp, target, dtype, anchors)
+    ref = oracle_mse({k: v.to(dtype) for k, v in inp.items()}, target.to(dtype), anchors)
+    # dL/dx = (2/N)(x - t) carries the float32 forward's position error (~1e-5 nm at these N)
+    # relative to x - t (~0.3 nm here), so the float32 parameter gradients of this loss are good
+    # to ~1e-4..1e-3 whatever computes them (the unfused sequence too: test_fused_equals_unfused)
+    tol = (1e-5, 2e-3) if dtype == torch.float32 else (1e-10, 1e-9)
+    assert rel(got[0], ref[0]) <= tol[0]
+    for a, b in zip(got[1:], ref[1:]):
+        assert rel(a, b) <= tol[1], rel(a, b)
+
+
+def test_fused_equals_unfused_sequence():
+    inp = nerf64.make_inputs(64, 513, seed=41)
+    target = target_for(inp, False, seed=42).float()
+    grad_loss = torch.rand(64, generator=torch.Generator().manual_seed(43))
+    got = fused(inp, target, torch.float32, False, grad_loss)
+    L, A, D = (inp[k].to(DEV).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    loss = ((cufk.reconstruct(L, A, D) - target.to(DEV)) ** 2).sum(-1).mean(-1)
+    loss.backward(grad_loss.to(DEV))
+    torch.testing.assert_close(got[0], loss.detach().cpu(), rtol=1e-5, atol=0)
+    for a, b in zip(got[1:], (L.grad, A.grad, D.grad)):
+        assert rel(a, b.cpu().double()) <= 1e-5
+
+
+def test_loss_without_gradients_is_the_same_loss():
+    inp = nerf64.make_inputs(20, 300, seed=44)
+    target = target_for(inp, False, seed=45).float().to(DEV)
+    L, A, D = (inp[k].to(DEV) for k in ("lengths", "angles", "dihedrals"))
+    no_grad = cufk.reconstruct_mse(L, A, D, target)
+    with_grad = cufk.reconstruct_mse(L.clone().requires_grad_(True), A, D, target)
+    assert torch.equal(no_grad, with_grad.detach())
+
+
+@pytest.mark.parametrize("case", ["near_pi_angle", "far_from_origin", "zero_bond"])
+def test_chains_taking_the_recompute_form_inside_the_fused_kernel(case):
+    inp = nerf64.make_inputs(6, 200, seed=46, anchors=True)
+    if case == "near_pi_angle":
+        inp["angles"][:, 50] = math.pi - 1e-3
+    elif case == "far_from_origin":
+        inp["p0"] = torch.tensor([300.0, -200.0, 100.0])
+    else:
+        inp["lengths"][:, 70] = 0.0
+    target = target_for(inp, True, seed=47)
+    got = fused(inp, target, torch.float64, True)
+    ref = oracle_mse({k: v.to(F64) for k, v in inp.items()}, target, True)
+    assert rel(got[0], ref[0]) <= 1e-10
+    for a, b in zip(got[1:], ref[1:]):
+        assert rel(a, b) <= 1e-8, rel(a, b)
+
+
+def test_single_chain_form():
+    inp = nerf64.make_inputs(1, 100, seed=48)
+    target = target_for(inp, False, seed=49).float()[0]
+    L, A, D = (inp[k][0].to(DEV).requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    loss = cufk.reconstruct_mse(L, A, D, target.to(DEV))
+    assert loss.dim() == 0
+    loss.backward()
+    assert L.grad.shape == L.shape and torch.isfinite(L.grad).all()
+
+
+def test_rejects_unsupported_inputs():
+    inp = nerf64.make_inputs(2, 20, seed=50)
+    L, A, D = (inp[k].to(DEV) for k in ("lengths", "angles", "dihedrals"))
+    t = torch.zeros(2, 20, 3, device=DEV)
+    with pytest.raises(RuntimeError, match="target gradients are not supported"):
+        cufk.reconstruct_mse(L, A, D, t.requires_grad_(True))
+    with pytest.raises(RuntimeError, match="float32 and float64"):
+        cufk.reconstruct_mse(L.half(), A.half(), D.half(), t.detach().half())
+    with pytest.raises(RuntimeError, match="target must have shape"):
+        cufk.reconstruct_mse(L, A, D, torch.zeros(2, 19, 3, device=DEV))
