@@ -1165,9 +1165,12 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   }
   V Fs[3], Ms[3];
   suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
-  // sweep: x1 = x_{s+1}, x2 = x_{s+2} carried (threads without steps read nothing)
+  // sweep: x1 = x_{s+1}, x2 = x_{s+2} and the torque about x_{s+2},
+  // tau_s = sum_{j >= s+3} (x_j - x_{s+2}) x g_j, carried from step to step as
+  // tau_{s+1} = tau_s - (x_{s+3} - x_{s+2}) x F_s (threads without steps read nothing)
   V x1[3] = {V(0), V(0), V(0)};
   V x2[3] = {V(0), V(0), V(0)};
+  V tau[3] = {V(0), V(0), V(0)};
   if (range.count > 0) {
     off = 3 * (range.first + 1);  // atoms first+1 and first+2 <= N-2
 #pragma unroll
@@ -1175,6 +1178,11 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
       x1[i] = cv.pos(off + i);
       x2[i] = cv.pos(off + 3 + i);
     }
+    const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+    V xf[3];
+    cross3(xr, Fs, xf);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tau[i] = vsub(Ms[i], xf[i]);
   }
   V dmin2 = V(1e30);
   off = 3 * (range.first + 3);
@@ -1186,18 +1194,15 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     const V d2 = dot3(d, d);
     dmin2 = fmin(dmin2, d2);
     const V inv = vrsqrt(d2);
-    const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
-    V xf[3];
-    cross3(xr, Fs, xf);
-    const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
     const V d_phi = vmul(dot3(d, tau), inv);
-    const V x3r[3] = {vsub(x3[0], o[0]), vsub(x3[1], o[1]), vsub(x3[2], o[2])};
-    V mx[3];
-    cross3(x3r, g, mx);
+    // tau -= (x3 - x2) x Fs, then Fs -= g
+    const V e[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+    tau[0] = vfma(e[2], Fs[1], vfma(vneg(e[1]), Fs[2], tau[0]));
+    tau[1] = vfma(e[0], Fs[2], vfma(vneg(e[2]), Fs[0], tau[1]));
+    tau[2] = vfma(e[1], Fs[0], vfma(vneg(e[0]), Fs[1], tau[2]));
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
       Fs[i] = vsub(Fs[i], g[i]);
-      Ms[i] = vsub(Ms[i], mx[i]);
       x1[i] = x2[i];
       x2[i] = x3[i];
     }
