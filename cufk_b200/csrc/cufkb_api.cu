@@ -357,7 +357,7 @@ template <typename T>
 int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* xyz, const void* g, void* graw,
                               int64_t grad_stride, int64_t batch, int points, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
-  const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
+  const size_t smem = cufkb::torsion_xyz_smem_bytes<T>(points);
   auto kernel = cufkb::torsion_backward_xyz_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackwardXyz, dtype_index<T>()), batch, points, smem)) return st;

@@ -95,6 +95,13 @@ __host__ __device__ inline size_t block_smem_bytes(int points, bool backward) {
   return bytes;
 }
 
+// The torsion xyz backward: the slots and the grad row of torsion_smem_bytes, and the raw row.
+template <typename T>
+__host__ __device__ inline size_t torsion_xyz_smem_bytes(int points) {
+  return slot_bytes(points, sizeof(typename ComputeOf<T>::type)) + staged_row_bytes(size_t(3) * points, sizeof(T)) +
+         staged_row_bytes(size_t(2) * (points - 3), sizeof(T));
+}
+
 template <typename T>
 __host__ __device__ inline size_t torsion_smem_bytes(int points, bool backward) {
   using R = typename ComputeOf<T>::type;
@@ -1112,11 +1119,11 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
 // Torsion backward from the forward's xyz (4- and 8-byte types), as the reference's own torsion
 // backward does (world_torsion_grad, torsion.cu:213-217 and :297-381): d phi_s = u_{s+1} . tau_s
 // with u_{s+1} the direction of bond (x_{s+1}, x_{s+2}) and tau_s = M_s - (x_{s+2} - o) x F_s, the
-// sums over atoms >= s+3 (moments about o = atom 2).  The xyz and grad rows are staged (16-byte
-// LDGSTS); d phi goes over the grad row; the last loop applies the raw-pair chain rule
-// d raw = d phi (c, -s) / n2 reading each raw element once from global memory, its partner (sin
-// or cos) from the neighbouring lane.  A bond shorter than 1e-3 |x|max, a pair below the norm
-// clamp (not a rotation), or a non-finite value sends the chain to the recompute form.
+// sums over atoms >= s+3 (moments about o = atom 2), carried from step to step.  The xyz, grad
+// and raw rows are staged (16-byte LDGSTS); d phi goes over the grad row; the last loop applies the
+// raw-pair chain rule d raw = d phi (c, -s) / n2 from the staged raw row.  A bond shorter than
+// 1e-3 |x|max, a pair below the norm clamp (not a rotation), or a non-finite value sends the chain
+// to the recompute form.
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_backward_xyz_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
@@ -1135,11 +1142,12 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const T* grow = grad_xyz + chain * 3 * N;
   unsigned char* const slot_region = smem;
   unsigned char* const grad_region = smem + slot_bytes(N, sizeof(R));
+  unsigned char* const raw_region = grad_region + staged_row_bytes(size_t(3) * N, sizeof(T));
   ChainViews<T> cv;
   cv.Y = stage_row_async(slot_region, xyz + chain * 3 * N, 3 * N, tid, nthr);
   cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
-  // the raw row is read once, by the chain-rule loop at the end: bring it into L2 meanwhile
-  for (int line = tid; line * 128 < 2 * St * int(sizeof(T)); line += nthr) prefetch_l2(reinterpret_cast<const char*>(raw) + line * 128);
+  // the raw row, read once by the chain-rule loop at the end, stages with the others
+  const T* raw_s = stage_row_async(raw_region, raw, 2 * St, tid, nthr);
   const StepRange range = step_range(tid, K, St);
   cp_async_wait_all();
   __syncthreads();
@@ -1214,26 +1222,21 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   bool redo = __syncthreads_or(bad) != 0;
   T* gr = grad_raw + chain * grad_stride;
   if (!redo) {
-    // chain rule, warp-uniform trip count so that every lane takes part in the shuffle.  A pair
-    // below the norm clamp is not normalised to a unit pair: that step is not a rotation, the
-    // positions cannot give its gradient, and the chain is redone below.
-    const int lane = tid & (kWarp - 1);
+    // chain rule from the staged raw row (each element and its partner, sin or cos, read from
+    // shared memory).  A pair below the norm clamp is not normalised to a unit pair: that step is
+    // not a rotation, the positions cannot give its gradient, and the chain is redone below.
     bool clamped = false;
-#pragma unroll 16  // the raw loads of 16 iterations in flight at once
-    for (int e0 = tid - lane; e0 < 2 * St; e0 += nthr) {
-      const int e = e0 + lane;
-      const bool live = e < 2 * St;
-      const V v = live ? to_r<V>(raw[e]) : V(1);
-      const V partner = shfl_xor(v, 1);
+#pragma unroll 4
+    for (int e = tid; e < 2 * St; e += nthr) {
+      const V v = to_r<V>(raw_s[e]);
+      const V partner = to_r<V>(raw_s[e ^ 1]);
       const V rs = (e & 1) ? partner : v;
       const V rc = (e & 1) ? v : partner;
       const V n2raw = vfma(rs, rs, vmul(rc, rc));
       clamped |= !(n2raw >= static_cast<V>(1.0e-8f * 1.0e-8f));
       const V rinv = torsion_rinv(torsion_norm2(rs, rc));
-      if (live) {
-        const V scale = vmul(cv.G[3 * ((e >> 1) + 3)], vmul(rinv, rinv));
-        gr[e] = from_r<T>((e & 1) ? vneg(vmul(rs, scale)) : vmul(rc, scale));
-      }
+      const V scale = vmul(cv.G[3 * ((e >> 1) + 3)], vmul(rinv, rinv));
+      gr[e] = from_r<T>((e & 1) ? vneg(vmul(rs, scale)) : vmul(rc, scale));
     }
     redo = __syncthreads_or(clamped) != 0;
   }
