@@ -196,20 +196,6 @@ __device__ __forceinline__ unsigned char* stage_block_inputs(ChainViews<T>& cv, 
   return p;
 }
 
-template <typename T>
-__device__ __forceinline__ void first_inputs(const ChainViews<T>& cv, typename ComputeOf<T>::type& l0, typename ComputeOf<T>::type& l1,
-                                             typename ComputeOf<T>::type& a0) {
-  if constexpr (sizeof(T) >= 4) {
-    l0 = cv.slot(3);
-    l1 = cv.slot(6);
-    a0 = cv.slot(7);
-  } else {
-    l0 = cv.staged(0, 0);
-    l1 = cv.staged(0, 1);
-    a0 = cv.staged(1, 0);
-  }
-}
-
 // World carry (F, p2) C: the frame in front of the thread's first step.
 template <typename V>
 __device__ __forceinline__ Affine<V> world_carry(const Affine<V>& carry, const V* F, const V* p2) {
