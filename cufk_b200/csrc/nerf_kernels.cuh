@@ -953,6 +953,44 @@ __device__ __forceinline__ void torsion_pair(const ChainViews<T>& cv, int s, typ
   }
 }
 
+// Sweep 1 of the torsion forward.  Step s takes its bond length and angle by phase (s % 3); the
+// thread rotates the three constant triples once, to its first step's phase, and walks its steps
+// three at a time, so that every step of an iteration uses fixed registers (no per-step modulo or
+// selects).
+// One step of the torsion forward sweep with its constants: local prefix advanced, its position
+// written to the step's slot.
+template <typename T, typename V, typename R>
+__device__ __forceinline__ void torsion_sweep_step(const ChainViews<T>& cv, Affine<V>& P, int s, R l, R st, R ct) {
+  V rs, rc;
+  torsion_pair<T>(cv, s, rs, rc);
+  const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+  advance(P, step_rot<V>(l, st, ct, vmul(rs, rinv), vmul(rc, rinv)));
+  const int off = 3 * (s + 3);
+  cv.set_slot(off, P.v[0]);
+  cv.set_slot(off + 1, P.v[1]);
+  cv.set_slot(off + 2, P.v[2]);
+}
+
+template <typename T, typename V, typename R>
+__device__ __forceinline__ Affine<V> torsion_sweep(const ChainViews<T>& cv, StepRange r, const TorsionConsts<R>& consts) {
+  R l0, l1, l2, s0, s1, s2, c0, c1, c2;
+  torsion_constants_for(consts, r.first, l0, s0, c0);
+  torsion_constants_for(consts, r.first + 1, l1, s1, c1);
+  torsion_constants_for(consts, r.first + 2, l2, s2, c2);
+  Affine<V> P = affine_identity<V>();
+  int s = r.first;
+  const int end = r.first + r.count;
+#pragma unroll 1
+  for (; s + 3 <= end; s += 3) {
+    torsion_sweep_step<T, V, R>(cv, P, s, l0, s0, c0);
+    torsion_sweep_step<T, V, R>(cv, P, s + 1, l1, s1, c1);
+    torsion_sweep_step<T, V, R>(cv, P, s + 2, l2, s2, c2);
+  }
+  if (s < end) torsion_sweep_step<T, V, R>(cv, P, s, l0, s0, c0);
+  if (s + 1 < end) torsion_sweep_step<T, V, R>(cv, P, s + 1, l1, s1, c1);
+  return P;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_forward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts, T* __restrict__ xyz,
@@ -989,17 +1027,8 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   cp_async_wait_all();
   __syncthreads();
 
-  auto step = [&](int s) {
-    V rs, rc;
-    torsion_pair<T>(cv, s, rs, rc);
-    const V rinv = torsion_rinv(torsion_norm2(rs, rc));
-    R l, st, ct;
-    torsion_constants_for(consts, s, l, st, ct);
-    return step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv));
-  };
-
   const StepRange range = step_range(tid, K, St);
-  const Affine<V> total = sweep_local_prefix<T, V>(cv, range, step);
+  const Affine<V> total = torsion_sweep<T, V, R>(cv, range, consts);
   const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
   apply_carry<T, V>(cv, W, range);
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
