@@ -1034,61 +1034,126 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 
+// One step of the torsion recompute form's sweep 1: local prefix advanced, the step's grad summed
+// into the thread's totals of g and Q = sum p (x) g (world coordinates).
+template <typename T, typename V, typename R>
+__device__ __forceinline__ void torsion_totals_step(const ChainViews<T>& cv, Affine<V>& P, int s, R l, R st, R ct, V (&gsum)[3], V (&Q)[9]) {
+  V rs, rc;
+  torsion_pair<T>(cv, s, rs, rc);
+  const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+  advance(P, step_rot<V>(l, st, ct, vmul(rs, rinv), vmul(rc, rinv)));
+  const int off = 3 * (s + 3);
+  const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+#pragma unroll
+  for (int c = 0; c < 3; ++c) gsum[c] = vadd(gsum[c], g[c]);
+#pragma unroll
+  for (int d = 0; d < 3; ++d) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) Q[3 * d + c] = vfma(P.v[d], g[c], Q[3 * d + c]);
+  }
+}
+
+// One step of the torsion recompute form's sweep 2: prefix from the carry, d phi from the running
+// force/moment suffix, the raw-pair chain rule d raw = d phi (c, -s) / n2 (torsion.cu:173-182)
+// into the step's slot.
+template <typename T, typename V, typename R>
+__device__ __forceinline__ void torsion_grad_step(const ChainViews<T>& cv, Affine<V>& P, int s, R l, R st, R ct, V (&Fs)[3], V (&Ms)[3]) {
+  const int off = 3 * (s + 3);
+  const V u0 = P.m[0], u1 = P.m[3], u2 = P.m[6];
+  const V xp[3] = {P.v[0], P.v[1], P.v[2]};
+  V rs, rc;
+  torsion_pair<T>(cv, s, rs, rc);
+  const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+  advance(P, step_rot<V>(l, st, ct, vmul(rs, rinv), vmul(rc, rinv)));
+  const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
+  V xf[3];
+  cross3(xp, Fs, xf);
+  const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
+  const V d_phi = vfma(u2, tau[2], vfma(u1, tau[1], vmul(u0, tau[0])));
+  V mx[3];
+  cross3(P.v, g, mx);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    Fs[i] = vsub(Fs[i], g[i]);
+    Ms[i] = vsub(Ms[i], mx[i]);
+  }
+  const V scale = vmul(d_phi, vmul(rinv, rinv));
+  cv.set_slot(off + 1, vmul(rc, scale));
+  cv.set_slot(off + 2, vneg(vmul(rs, scale)));
+}
+
 // Recompute form of the torsion backward after staging (raw pairs in the slots or a staged row,
 // grad row in cv.G): the same structure as the block recompute form; d raw goes into the slots.
-template <typename T, typename V, typename R>
+// kRotate: both sweeps take their constants as torsion_sweep does (rotated once to the thread's
+// first step's phase, three steps per iteration), at the cost of nine more live registers; the
+// xyz form's fallback, which shares its kernel's register budget, picks them per step instead.
+template <typename T, typename V, typename R, bool kRotate = true>
 __device__ __forceinline__ void torsion_backward_recompute(const ChainViews<T>& cv, CtaExchange<V>& ex, const TorsionConsts<R>& consts, StepRange range,
                                                            int nwarps) {
   V F[9], p1[3], p2[3];
   torsion_base<V>(consts, F, p1, p2);
-  auto step = [&](int s) {
-    V rs, rc;
-    torsion_pair<T>(cv, s, rs, rc);
-    const V rinv = torsion_rinv(torsion_norm2(rs, rc));
-    R l, st, ct;
-    torsion_constants_for(consts, s, l, st, ct);
-    return step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv));
-  };
-  // the fixed torsion base frame is orthonormal: world coordinates throughout
-  V gsum[3];
-  V Q[9];
-  const Affine<V> total = sweep_backward_totals<true, T, V>(cv, F, range, step, gsum, Q);
-  const Affine<V> carry = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
-  V msum[3];
-  moment_total<V>(carry, gsum, Q, msum);
-  V Fs[3], Ms[3];
-  suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
-
-  Affine<V> P = carry;
-  int off = 3 * (range.first + 3);
-#pragma unroll 2
-  for (int k = 0; k < range.count; ++k, off += 3) {
-    const int s = range.first + k;
-    const V u0 = P.m[0], u1 = P.m[3], u2 = P.m[6];
-    const V xp[3] = {P.v[0], P.v[1], P.v[2]};
-    V rs, rc;
-    torsion_pair<T>(cv, s, rs, rc);
-    const V n2 = torsion_norm2(rs, rc);
-    const V rinv = torsion_rinv(n2);
-    R l, st, ct;
-    torsion_constants_for(consts, s, l, st, ct);
-    advance(P, step_rot(l, st, ct, vmul(rs, rinv), vmul(rc, rinv)));
-    const V g[3] = {cv.grad(off), cv.grad(off + 1), cv.grad(off + 2)};
-    V xf[3];
-    cross3(xp, Fs, xf);
-    const V tau[3] = {vsub(Ms[0], xf[0]), vsub(Ms[1], xf[1]), vsub(Ms[2], xf[2])};
-    const V d_phi = vfma(u2, tau[2], vfma(u1, tau[1], vmul(u0, tau[0])));
-    V mx[3];
-    cross3(P.v, g, mx);
+  if constexpr (!kRotate) {
+    V gsum[3] = {V(0), V(0), V(0)};
+    V Q[9];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      Fs[i] = vsub(Fs[i], g[i]);
-      Ms[i] = vsub(Ms[i], mx[i]);
+    for (int i = 0; i < 9; ++i) Q[i] = V(0);
+    Affine<V> P = affine_identity<V>();
+    const int end = range.first + range.count;
+#pragma unroll 2
+    for (int s = range.first; s < end; ++s) {
+      R l, st, ct;
+      torsion_constants_for(consts, s, l, st, ct);
+      torsion_totals_step<T, V, R>(cv, P, s, l, st, ct, gsum, Q);
     }
-    // raw-pair chain rule (torsion.cu:173-182): d raw = d phi * (c, -s) / n2
-    const V scale = vmul(d_phi, vmul(rinv, rinv));
-    cv.set_slot(off + 1, vmul(rc, scale));
-    cv.set_slot(off + 2, vneg(vmul(rs, scale)));
+    const Affine<V> carry = world_carry(cta_exclusive_affine<V>(P, ex.warp_totals, nwarps), F, p2);
+    V msum[3];
+    moment_total<V>(carry, gsum, Q, msum);
+    V Fs[3], Ms[3];
+    suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
+    P = carry;
+#pragma unroll 2
+    for (int s = range.first; s < end; ++s) {
+      R l, st, ct;
+      torsion_constants_for(consts, s, l, st, ct);
+      torsion_grad_step<T, V, R>(cv, P, s, l, st, ct, Fs, Ms);
+    }
+  } else {
+    R l0, l1, l2, s0, s1, s2, c0, c1, c2;
+    torsion_constants_for(consts, range.first, l0, s0, c0);
+    torsion_constants_for(consts, range.first + 1, l1, s1, c1);
+    torsion_constants_for(consts, range.first + 2, l2, s2, c2);
+    const int end = range.first + range.count;
+    // the fixed torsion base frame is orthonormal: world coordinates throughout
+    V gsum[3] = {V(0), V(0), V(0)};
+    V Q[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) Q[i] = V(0);
+    Affine<V> P = affine_identity<V>();
+    int s = range.first;
+#pragma unroll 1
+    for (; s + 3 <= end; s += 3) {
+      torsion_totals_step<T, V, R>(cv, P, s, l0, s0, c0, gsum, Q);
+      torsion_totals_step<T, V, R>(cv, P, s + 1, l1, s1, c1, gsum, Q);
+      torsion_totals_step<T, V, R>(cv, P, s + 2, l2, s2, c2, gsum, Q);
+    }
+    if (s < end) torsion_totals_step<T, V, R>(cv, P, s, l0, s0, c0, gsum, Q);
+    if (s + 1 < end) torsion_totals_step<T, V, R>(cv, P, s + 1, l1, s1, c1, gsum, Q);
+    const Affine<V> carry = world_carry(cta_exclusive_affine<V>(P, ex.warp_totals, nwarps), F, p2);
+    V msum[3];
+    moment_total<V>(carry, gsum, Q, msum);
+    V Fs[3], Ms[3];
+    suffix_base<V>(gsum, msum, ex, nwarps, Fs, Ms);
+
+    P = carry;
+    s = range.first;
+#pragma unroll 1
+    for (; s + 3 <= end; s += 3) {
+      torsion_grad_step<T, V, R>(cv, P, s, l0, s0, c0, Fs, Ms);
+      torsion_grad_step<T, V, R>(cv, P, s + 1, l1, s1, c1, Fs, Ms);
+      torsion_grad_step<T, V, R>(cv, P, s + 2, l2, s2, c2, Fs, Ms);
+    }
+    if (s < end) torsion_grad_step<T, V, R>(cv, P, s, l0, s0, c0, Fs, Ms);
+    if (s + 1 < end) torsion_grad_step<T, V, R>(cv, P, s + 1, l1, s1, c1, Fs, Ms);
   }
 }
 
@@ -1263,7 +1328,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     cv.G = stage_row_async(grad_region, grow, 3 * N, tid, nthr);
     cp_async_wait_all();
     __syncthreads();
-    torsion_backward_recompute<T, V, R>(cv, ex, consts, range, nwarps);
+    torsion_backward_recompute<T, V, R, false>(cv, ex, consts, range, nwarps);
     __syncthreads();
     write_pair_grads<T, R>(cv.X, gr, St, tid, nthr);
   }
