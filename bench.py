@@ -1,9 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the cufk reconstruction hot path on B200: fwd+bwd atoms/s (B=4096, N=768, fp32).
 
-One step = the block forward plus the block backward over this rank's shard of config 1
-(B = 4096 chains split evenly over the ranks, N = 768 atoms, float32).  Prints ONE JSON line on
-rank 0.
+One step = the block forward plus the block backward over this rank's chains of config 1
+(B = 4096 chains per rank by default, N = 768 atoms, float32).  Prints ONE JSON line on rank 0.
 
 * ``value``: atoms of all ranks / (max over ranks of the device time per step).  Inputs are
   resident in HBM.  Each step replays a CUDA graph holding the two kernel launches for one of
@@ -19,9 +18,11 @@ rank 0.
 * ``--impl reference``: the reference arm.  The reference's path exists only as CUDA kernels, so
   the CPU implementation timed is the float64 restatement of its algorithm on all host cores.
 
-Multi-GPU: ``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``; the batch
-is sharded by chains with no collective on the hot path (strong scaling of the fixed B = 4096);
-an NCCL all-gather of xyz is timed separately and reported under ``allgather``.
+Multi-GPU: ``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``.  Chains are
+independent, so there is no collective on the hot path.  ``--scaling weak`` (the default) gives
+every rank a full B = 4096 set of its own chains (seed = rank), so the job grows with N;
+``--scaling strong`` splits the fixed B = 4096 over the ranks.  An NCCL all-gather of xyz is timed
+separately and reported under ``allgather``.
 """
 
 from __future__ import annotations
@@ -68,7 +69,13 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global number of chains")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="chains per rank (weak) or in total (strong)")
+    ap.add_argument(
+        "--scaling",
+        choices=["weak", "strong"],
+        default="weak",
+        help="weak: every rank runs the whole batch on its own chains; strong: the batch is split over the ranks",
+    )
     ap.add_argument("--points", type=int, default=POINTS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -149,6 +156,17 @@ def shard(batch: int, world: int, rank: int) -> tuple[int, int]:
     per, extra = divmod(batch, world)
     lo = rank * per + min(rank, extra)
     return lo, lo + per + (1 if rank < extra else 0)
+
+
+def rank_inputs(make, batch: int, scaling: str, world: int, rank: int) -> tuple[dict, int]:
+    """This rank's inputs and the job's total chain count.  Weak scaling: a whole `batch` of the
+    rank's own chains (generated from seed = rank).  Strong: the rank's slice of one `batch`
+    generated from seed 0 (identically on every rank).  `make(batch, seed)` builds the inputs."""
+    if scaling == "weak" or world == 1:
+        return make(batch, rank), batch * world
+    lo, hi = shard(batch, world, rank)
+    host = make(batch, 0)
+    return {k: (v[lo:hi].contiguous() if v.dim() > 1 else v) for k, v in host.items()}, batch
 
 
 # ------------------------------------------------------------------------------------------------
@@ -274,13 +292,10 @@ def run_ours(args, dist: Dist) -> dict | None:
 
     C = _native._C
     dev = torch.device("cuda", torch.cuda.current_device())
-    lo, hi = shard(args.batch, dist.world, dist.rank)
-    b_local = hi - lo
     n = args.points
-
-    # synthetic config-1 inputs: the global batch is generated identically on every rank from seed 0
-    host = make_inputs(args.batch, n, seed=0)
-    host = {k: v[lo:hi].contiguous() for k, v in host.items()}
+    # synthetic config-1 inputs of this rank
+    host, global_batch = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, args.scaling, dist.world, dist.rank)
+    b_local = host["lengths"].shape[0]
     set_bytes = 4 * b_local * ((n - 1) + (n - 2) + (n - 3) + 3 * n) * 2  # inputs + outputs of a step
     n_sets = max(2, min(64, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
     sets = []
@@ -324,7 +339,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         ms_fwd = time_graphs(graphs_fwd, args.steps, args.warmup, dist, stream) / args.steps
         ms_bwd = time_graphs(graphs_bwd, args.steps, args.warmup, dist, stream) / args.steps
     ms_step = ms_total / args.steps
-    atoms_total = args.batch * n
+    atoms_total = global_batch * n
     value = atoms_total / (ms_step * 1e-3)
 
     # roofline of the dominant kernel
@@ -394,7 +409,7 @@ def run_ours(args, dist: Dist) -> dict | None:
     # end to end through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(cufk, host, dev, args, dist)
+        e2e = run_e2e(cufk, host, dev, args, dist, global_batch)
 
     result = {
         "metric": METRIC,
@@ -405,16 +420,18 @@ def run_ours(args, dist: Dist) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": ms_step,
         "higher_is_better": True,
-        "scaling": "strong",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded backbone internal coordinates, oracle/nerf64.make_inputs)",
         "config": {
-            "workload": "config 1: block reconstruct forward+backward, B=4096 chains (global), N=768 atoms, fp32",
-            "global_batch": args.batch,
+            "workload": "config 1: block reconstruct forward+backward, B=4096 chains per GPU, N=768 atoms, fp32"
+            if args.scaling == "weak"
+            else "config 1: block reconstruct forward+backward, B=4096 chains split over the GPUs, N=768 atoms, fp32",
+            "global_batch": global_batch,
             "points": n,
             "per_gpu_batch": b_local,
-            "parallelism": f"batch-sharded x{dist.world}, no collective on the hot path",
+            "parallelism": f"chains independent, {'each rank its own B' if args.scaling == 'weak' else 'one B split'} x{dist.world}; no collective on the hot path",
             "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB > L2 (126 MB)",
             "timing": "one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks",
         },
@@ -431,7 +448,7 @@ def run_ours(args, dist: Dist) -> dict | None:
     return result
 
 
-def run_e2e(cufk, host, dev, args, dist: Dist) -> dict:
+def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     """The metric through the public API with host buffers: every step copies the inputs and the
     grad host->device from pinned memory, runs ``cufk_b200.reconstruct`` + ``backward`` and copies
     xyz and the three gradients device->host.  Copy-in, compute and copy-out are on three streams,
@@ -496,7 +513,7 @@ def run_e2e(cufk, host, dev, args, dist: Dist) -> dict:
     ref = cufk.reconstruct(pinned["lengths"].to(dev), pinned["angles"].to(dev), pinned["dihedrals"].to(dev))
     assert torch.equal(outs["xyz"], ref.cpu()), "e2e output mismatch"
     return {
-        "value": args.batch * args.points / (ms * 1e-3),
+        "value": global_batch * args.points / (ms * 1e-3),
         "unit": "atoms/s",
         "h2d_bytes_per_step": h2d,
         "d2h_bytes_per_step": d2h,
@@ -577,22 +594,22 @@ def run_workload(args, dist: Dist) -> dict:
     C = _native._C
     kind, batch, points, dtype, anchors = WORKLOADS[args.workload]
     dev = torch.device("cuda", torch.cuda.current_device())
-    lo, hi = shard(batch, dist.world, dist.rank)
-    host = workload_inputs(kind, batch, points, dtype, anchors, seed=0)
-    host = {k: (v[lo:hi].contiguous() if v.dim() > 1 else v) for k, v in host.items()}
+    host, global_batch = rank_inputs(
+        lambda b, seed: workload_inputs(kind, b, points, dtype, anchors, seed=seed), batch, args.scaling, dist.world, dist.rank
+    )
     elem = torch.empty(0, dtype=dtype).element_size()
-    b_local = hi - lo
+    b_local = host["grad" if "grad" in host else "target"].shape[0]
     steps_s = points - 3
     if kind == "block":
         fwd_b, bwd_b = (6 * points - 6) * elem, (9 * points - 12) * elem
-        names = ("block_forward_kernel", "block_backward_xyz_kernel" if elem >= 4 else "block_backward_kernel")
+        names = ("block_forward_kernel", "block_backward_xyz_kernel" if elem >= 4 else "block_backward_lp_kernel")
     elif kind == "mse":
         # one kernel: read lengths/angles/dihedrals and the target, write the three gradient rows
         fwd_b, bwd_b = (9 * points - 12) * elem, 0
         names = ("block_mse_kernel", None)
     else:
         fwd_b, bwd_b = (2 * steps_s + 3 * points) * elem, (4 * steps_s + 3 * points) * elem
-        names = ("torsion_forward_kernel", "torsion_backward_xyz_kernel" if elem >= 4 else "torsion_backward_kernel")
+        names = ("torsion_forward_kernel", "torsion_backward_xyz_kernel" if elem >= 4 else "torsion_backward_lp_kernel")
     set_bytes = b_local * (fwd_b + bwd_b)
     n_sets = max(2, min(16, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
     consts = torsion_constants(BACKBONE_LENGTHS, BACKBONE_ANGLES)
@@ -674,21 +691,21 @@ def run_workload(args, dist: Dist) -> dict:
     dom = max(per_kernel, key=lambda k: per_kernel[k]["launch_ms"])
     return {
         "metric": f"fwd+bwd atoms/s ({args.workload}: {kind}, B={batch}, N={points}, {str(dtype).replace('torch.', '')})",
-        "value": batch * points / (ms_step * 1e-3),
+        "value": global_batch * points / (ms_step * 1e-3),
         "unit": "atoms/s",
         "n_gpus": dist.world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms_step,
         "higher_is_better": True,
-        "scaling": "strong",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": {torch.float32: "f32", torch.float64: "f64", torch.float16: "f16", torch.bfloat16: "bf16"}[dtype],
         "data": "synthetic (seeded, the distributions of the configuration)",
         "config": {
             "workload": args.workload,
             "kind": kind,
-            "global_batch": batch,
+            "global_batch": global_batch,
             "points": points,
             "anchors": anchors,
             "per_gpu_batch": b_local,
@@ -743,13 +760,13 @@ def run_reference(args) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": dt * 1e3,
         "higher_is_better": True,
-        "scaling": "strong",
+        "scaling": args.scaling,
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic (seeded backbone internal coordinates)",
         "config": {
             "workload": "config 1: block reconstruct forward+backward, B=4096 chains, N=768 atoms",
-            "global_batch": args.batch,
+            "global_batch": args.batch * (world if args.scaling == "weak" else 1),
             "points": args.points,
             "implementation": "the reference path has no CPU code; its algorithm restated in float64 torch (oracle/nerf64.py)",
         },

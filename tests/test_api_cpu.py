@@ -81,3 +81,22 @@ def test_shards_cover_the_batch():
         assert all(ranges[i][1] == ranges[i + 1][0] for i in range(world - 1))
         sizes = [hi - lo for lo, hi in ranges]
         assert max(sizes) - min(sizes) <= 1
+
+
+def test_rank_inputs_weak_and_strong():
+    import bench
+
+    make = lambda b, seed: bench.make_inputs(b, 20, seed=seed)  # noqa: E731
+    # weak: every rank a whole batch of its own chains; the job is world x batch
+    w0, total = bench.rank_inputs(make, 6, "weak", 2, 0)
+    w1, _ = bench.rank_inputs(make, 6, "weak", 2, 1)
+    assert total == 12 and w0["lengths"].shape[0] == 6 and w1["lengths"].shape[0] == 6
+    assert not torch.equal(w0["dihedrals"], w1["dihedrals"])
+    # strong: the ranks' slices of one batch
+    whole = make(7, 0)
+    parts = [bench.rank_inputs(make, 7, "strong", 2, r) for r in range(2)]
+    assert all(t == 7 for _, t in parts)
+    for k in whole:
+        assert torch.equal(torch.cat([p[k] for p, _ in parts]), whole[k])
+    # one rank: the same either way
+    assert torch.equal(bench.rank_inputs(make, 5, "weak", 1, 0)[0]["grad"], bench.rank_inputs(make, 5, "strong", 1, 0)[0]["grad"])
