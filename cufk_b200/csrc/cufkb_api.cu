@@ -34,8 +34,30 @@ constexpr int kMinItems = 5;      // never split a chain below this many steps p
 #ifndef CUFKB_XYZ_TARGET_WARPS_PER_SM
 #define CUFKB_XYZ_TARGET_WARPS_PER_SM 20
 #endif
+// The torsion kernels aim lower too: with fewer warps per chain their scans cost less than the
+// residency they give up (B200, config 3 fp32: forward 57.7 vs 67.7 us, xyz backward 108.4 vs
+// 116.9 us at 16 against 32).
+#ifndef CUFKB_TORSION_TARGET_WARPS_PER_SM
+#define CUFKB_TORSION_TARGET_WARPS_PER_SM 16
+#endif
+// The 16-bit kernels aim lowest.  Their slots hold float results next to the staged 16-bit rows, so
+// a chain needs more shared memory and the default target splits it over more warps (4 at N=1026),
+// whose affine scan then costs more than the extra residency hides (B200, config 4: block forward
+// 69.8 vs 83.4 us, recompute backward 136.0 vs 149.3 us; config 3 bf16: torsion backward 114.8 vs
+// 121.5 us at 12 against 32).
+#ifndef CUFKB_TARGET_WARPS_PER_SM_16BIT
+#define CUFKB_TARGET_WARPS_PER_SM_16BIT 12
+#endif
 constexpr int kTargetWarpsPerSm = CUFKB_TARGET_WARPS_PER_SM;
 constexpr int kXyzTargetWarpsPerSm = CUFKB_XYZ_TARGET_WARPS_PER_SM;
+constexpr int kTorsionTargetWarpsPerSm = CUFKB_TORSION_TARGET_WARPS_PER_SM;
+constexpr int kTargetWarpsPerSm16 = CUFKB_TARGET_WARPS_PER_SM_16BIT;
+
+// The resident-warp target of a kernel for element type T whose 32/64-bit target is `wide`.
+template <typename T>
+constexpr int target_warps(int wide) {
+  return sizeof(T) == 2 ? kTargetWarpsPerSm16 : wide;
+}
 // Warps per SM the block forward's grid must offer before a small batch stops splitting its chains
 // over more warps.  Each extra warp adds scan work; on B200 at N=768 two warps per chain beat three
 // to five at 1024 and 2048 chains, and four match them at 512 (per-launch times 12.3 vs 14.3 us and
@@ -250,7 +272,7 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kBlockForward, dtype_index<T>()), batch, points, smem, kTargetWarpsPerSm, kForwardFillWarpsPerSm)) {
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockForward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTargetWarpsPerSm), kForwardFillWarpsPerSm)) {
     return st;
   }
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
@@ -267,7 +289,7 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackward, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kBlockBackward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTargetWarpsPerSm))) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
@@ -329,7 +351,7 @@ int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsio
   const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
   auto kernel = cufkb::torsion_forward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kTorsionForward, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionForward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTorsionTargetWarpsPerSm))) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c), static_cast<T*>(xyz),
                                                                           geo);
@@ -344,7 +366,7 @@ int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsi
   const size_t smem = cufkb::torsion_smem_bytes<T>(points, true);
   auto kernel = cufkb::torsion_backward_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackward, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTorsionTargetWarpsPerSm))) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                           static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
@@ -360,7 +382,7 @@ int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_t
   const size_t smem = cufkb::torsion_xyz_smem_bytes<T>(points);
   auto kernel = cufkb::torsion_backward_xyz_kernel<T>;
   LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackwardXyz, dtype_index<T>()), batch, points, smem)) return st;
+  if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackwardXyz, dtype_index<T>()), batch, points, smem, kTorsionTargetWarpsPerSm)) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                           static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(graw),
