@@ -816,6 +816,12 @@ def main(argv=None) -> int:
         if out is not None:
             print(json.dumps(out), flush=True)
         return 0
+    # The JSON line is the only thing this process writes to its stdout: libraries that print there
+    # from native code (NCCL's version line under NCCL_DEBUG=VERSION, for one) write to stderr while
+    # the step runs, through a file descriptor 1 pointed at stderr.
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     dist = Dist(args.gpus)
     try:
         out = run_ours(args, dist) if args.workload == "cfg1" else run_workload(args, dist)
@@ -823,7 +829,8 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         dist.close()
     if dist.rank == 0 and out is not None:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=json_out, flush=True)
+    json_out.close()
     return 0
 
 
