@@ -19,10 +19,14 @@ One step = the block forward plus the block backward over this rank's chains of 
   the CPU implementation timed is the float64 restatement of its algorithm on all host cores.
 
 Multi-GPU: ``python -m torch.distributed.run --nproc-per-node N bench.py --gpus N``.  Chains are
-independent, so there is no collective on the hot path.  ``--scaling weak`` (the default) gives
-every rank a full B = 4096 set of its own chains (seed = rank), so the job grows with N;
-``--scaling strong`` splits the fixed B = 4096 over the ranks.  An NCCL all-gather of xyz is timed
-separately and reported under ``allgather``.
+independent, so there is no collective on the hot path.  ``--scaling strong`` (the default, config
+1's own split) divides the fixed B = 4096 over the ranks (2048 / 1024 / 512 chains per GPU at
+2 / 4 / 8); the line also carries the weak figure (every rank a full B = 4096 of its own chains)
+under ``weak``.  ``--scaling weak`` makes weak the headline instead.  An NCCL all-gather of xyz is
+timed separately and reported under ``allgather``.
+
+Timing: every timed region is repeated (``--repeats``, default 5) and the median is reported, with
+the spread beside it; ``unflushed`` is the same step replayed on one resident input set.
 """
 
 from __future__ import annotations
@@ -73,9 +77,11 @@ def parse_args(argv=None):
     ap.add_argument(
         "--scaling",
         choices=["weak", "strong"],
-        default="weak",
-        help="weak: every rank runs the whole batch on its own chains; strong: the batch is split over the ranks",
+        default="strong",
+        help="strong (config 1's split): the batch is split over the ranks; weak: every rank runs the whole batch on its own chains",
     )
+    ap.add_argument("--repeats", type=int, default=5, help="timed regions per figure (median reported)")
+    ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's own kernels (oracle/_ref)")
     ap.add_argument("--points", type=int, default=POINTS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -127,6 +133,15 @@ class Dist:
         t = torch.tensor([value], dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def gather(self, values: list[float]) -> list[list[float]]:
+        """Every rank's `values` (same length on all ranks), indexed by rank."""
+        if self.pg is None:
+            return [list(values)]
+        t = torch.tensor(values, dtype=torch.float64, device=self.device)
+        out = torch.empty(self.world * len(values), dtype=torch.float64, device=self.device)
+        self.pg.all_gather_into_tensor(out, t)
+        return out.view(self.world, len(values)).tolist()
 
     def close(self):
         if self.pg is not None:
@@ -266,23 +281,77 @@ def profiled_traffic_per_atom(kernel: str):
     return None if entry is None else float(entry["dram_bytes_per_atom"])
 
 
-def time_graphs(graphs, steps: int, warmup: int, dist: Dist, stream) -> float:
-    """Replays graphs[k % len] for `warmup` then `steps` iterations; returns max-over-ranks ms."""
+def time_graphs(graphs, steps: int, warmup: int, dist: Dist, stream, repeats: int = 1) -> list[float]:
+    """Replays graphs[k % len] for `warmup` then, `repeats` times, `steps` iterations bracketed by
+    a barrier and a device synchronisation; returns the max-over-ranks ms of each repeat."""
     for k in range(warmup):
         graphs[k % len(graphs)].replay()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for k in range(steps):
-        graphs[k % len(graphs)].replay()
-    end.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    return dist.max(start.elapsed_time(end))
+    out = []
+    for _ in range(max(1, repeats)):
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for k in range(steps):
+            graphs[k % len(graphs)].replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        out.append(dist.max(start.elapsed_time(end)))
+    return out
+
+
+def spread(ms_per_step: list[float]) -> dict:
+    """Median, min and max of per-step times (ms) over the repeats."""
+    return {
+        "median_ms": statistics.median(ms_per_step),
+        "min_ms": min(ms_per_step),
+        "max_ms": max(ms_per_step),
+        "repeats": len(ms_per_step),
+    }
+
+
+class StepGraphs:
+    """Device-resident input sets of one rank and one CUDA graph per set for the step (forward then
+    the backward that reads the forward's xyz, the kernels autograd runs) and for each kernel alone.
+    The sets rotate (total footprint > 3x the 126 MB L2) so that every step reads from HBM."""
+
+    def __init__(self, C, host: dict, n: int, dev, stream):
+        b_local = host["lengths"].shape[0]
+        self.b_local = b_local
+        self.set_bytes = 4 * b_local * ((n - 1) + (n - 2) + (n - 3) + 3 * n) * 2  # inputs + outputs of a step
+        self.n_sets = max(2, min(64, math.ceil(3 * L2_BYTES / max(self.set_bytes, 1))))
+        self.sets = []
+        for i in range(self.n_sets):
+            # each set a distinct copy (perturbed dihedrals) so no two sets alias
+            d = {k: v.to(dev) for k, v in host.items()}
+            d["dihedrals"] = d["dihedrals"] + 1e-3 * i
+            self.sets.append(d)
+        torch.cuda.synchronize()
+        self.step, self.fwd, self.bwd = [], [], []
+        with torch.cuda.stream(stream):
+            for d in self.sets:  # eager warm-up of both kernels (first-call attribute setup happens here)
+                d["xyz"] = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
+            stream.synchronize()
+            for d in self.sets:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    xyz = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                    C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, d["grad"])
+                self.step.append(g)
+                gf = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gf, stream=stream):
+                    C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+                self.fwd.append(gf)
+                gb = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gb, stream=stream):
+                    C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
+                self.bwd.append(gb)
+        torch.cuda.synchronize()
 
 
 def run_ours(args, dist: Dist) -> dict | None:
@@ -293,54 +362,44 @@ def run_ours(args, dist: Dist) -> dict | None:
     C = _native._C
     dev = torch.device("cuda", torch.cuda.current_device())
     n = args.points
-    # synthetic config-1 inputs of this rank
-    host, global_batch = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, args.scaling, dist.world, dist.rank)
-    b_local = host["lengths"].shape[0]
-    set_bytes = 4 * b_local * ((n - 1) + (n - 2) + (n - 3) + 3 * n) * 2  # inputs + outputs of a step
-    n_sets = max(2, min(64, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
-    sets = []
-    for i in range(n_sets):
-        # each set a distinct copy (perturbed dihedrals) so no two sets alias
-        d = {k: v.to(dev) for k, v in host.items()}
-        d["dihedrals"] = d["dihedrals"] + 1e-3 * i
-        sets.append(d)
-    torch.cuda.synchronize()
-
-    # The step is what cufk_b200.reconstruct + autograd runs: the forward, then the backward that
-    # reads the forward's xyz (float32).
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
-    graphs_step, graphs_fwd, graphs_bwd = [], [], []
-    with torch.cuda.stream(stream):
-        for d in sets:  # eager warm-up of both kernels (first-call attribute setup happens here)
-            d["xyz"] = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-            C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
-        stream.synchronize()
-        for d in sets:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                xyz = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, d["grad"])
-            graphs_step.append(g)
-            gf = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gf, stream=stream):
-                C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-            graphs_fwd.append(gf)
-            gb = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gb, stream=stream):
-                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
-            graphs_bwd.append(gb)
-    torch.cuda.synchronize()
+    # synthetic config-1 inputs of this rank: the headline split, and (several ranks) the other one
+    host, global_batch = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, args.scaling, dist.world, dist.rank)
+    sg = StepGraphs(C, host, n, dev, stream)
+    b_local = sg.b_local
 
     sampler = ClockSampler(dev.index)
     with torch.cuda.stream(stream):
         with sampler:
-            ms_total = time_graphs(graphs_step, args.steps, args.warmup, dist, stream)
-        ms_fwd = time_graphs(graphs_fwd, args.steps, args.warmup, dist, stream) / args.steps
-        ms_bwd = time_graphs(graphs_bwd, args.steps, args.warmup, dist, stream) / args.steps
-    ms_step = ms_total / args.steps
+            step_ms = [t / args.steps for t in time_graphs(sg.step, args.steps, args.warmup, dist, stream, args.repeats)]
+        fwd_ms = [t / args.steps for t in time_graphs(sg.fwd, args.steps, args.warmup, dist, stream, args.repeats)]
+        bwd_ms = [t / args.steps for t in time_graphs(sg.bwd, args.steps, args.warmup, dist, stream, args.repeats)]
+        # the same step on one resident input set (the inputs of a step may still be in L2)
+        unflushed_ms = [t / args.steps for t in time_graphs(sg.step[:1], args.steps, args.warmup, dist, stream, args.repeats)]
+    ms_step = statistics.median(step_ms)
+    ms_fwd, ms_bwd = statistics.median(fwd_ms), statistics.median(bwd_ms)
     atoms_total = global_batch * n
     value = atoms_total / (ms_step * 1e-3)
+
+    # the other scaling mode on several ranks (weak beside a strong headline, or strong beside weak)
+    other = None
+    if dist.world > 1:
+        other_mode = "weak" if args.scaling == "strong" else "strong"
+        host_o, global_o = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, other_mode, dist.world, dist.rank)
+        sg_o = StepGraphs(C, host_o, n, dev, stream)
+        with torch.cuda.stream(stream):
+            o_ms = [t / args.steps for t in time_graphs(sg_o.step, args.steps, args.warmup, dist, stream, args.repeats)]
+        other = {
+            "scaling": other_mode,
+            "value": global_o * n / (statistics.median(o_ms) * 1e-3),
+            "ms_per_step": statistics.median(o_ms),
+            "global_batch": global_o,
+            "per_gpu_batch": sg_o.b_local,
+            "spread": spread(o_ms),
+        }
+        del sg_o
+        torch.cuda.synchronize()
 
     # roofline of the dominant kernel
     peak, peak_kind = measured_peak()
@@ -376,8 +435,9 @@ def run_ours(args, dist: Dist) -> dict | None:
                 "frac": round(b * atoms_local / (t * 1e-3) / 1e9 / peak, 4),
                 "moved_bytes_per_atom": round(moved_bpa[k], 3),
                 "moved_gbs": round(moved_bpa[k] * atoms_local / (t * 1e-3) / 1e9, 1),
+                "spread": spread(ms),
             }
-            for k, (t, b) in per_kernel.items()
+            for (k, (t, b)), ms in zip(per_kernel.items(), (fwd_ms, bwd_ms))
         },
         "step_frac": round((fwd_bpa + bwd_bpa) * atoms_local / (ms_step * 1e-3) / 1e9 / peak, 4),
     }
@@ -406,11 +466,20 @@ def run_ours(args, dist: Dist) -> dict | None:
             "bus_gbs": round(nbytes * (dist.world - 1) / dist.world / (ms_ag * 1e-3) / 1e9, 1),
         }
 
+    # the reference's own kernels on the same box (single-GPU runs only)
+    ref_kernels = None
+    if dist.world == 1 and not args.no_ref_kernels:
+        ref_kernels = time_reference_kernels(cufk, sg, n, stream, args)
+
     # end to end through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(cufk, host, dev, args, dist, global_batch)
 
+    workload = {
+        "strong": "config 1: block reconstruct forward+backward, B=4096 chains split over the GPUs, N=768 atoms, fp32",
+        "weak": "config 1: block reconstruct forward+backward, B=4096 chains per GPU, N=768 atoms, fp32",
+    }[args.scaling if dist.world > 1 else "strong"]
     result = {
         "metric": METRIC,
         "value": value,
@@ -420,32 +489,88 @@ def run_ours(args, dist: Dist) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": ms_step,
         "higher_is_better": True,
-        "scaling": args.scaling,
+        "scaling": args.scaling if dist.world > 1 else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded backbone internal coordinates, oracle/nerf64.make_inputs)",
         "config": {
-            "workload": "config 1: block reconstruct forward+backward, B=4096 chains per GPU, N=768 atoms, fp32"
-            if args.scaling == "weak"
-            else "config 1: block reconstruct forward+backward, B=4096 chains split over the GPUs, N=768 atoms, fp32",
+            "workload": workload,
             "global_batch": global_batch,
             "points": n,
             "per_gpu_batch": b_local,
-            "parallelism": f"chains independent, {'each rank its own B' if args.scaling == 'weak' else 'one B split'} x{dist.world}; no collective on the hot path",
-            "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB > L2 (126 MB)",
-            "timing": "one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks",
+            "parallelism": f"chains independent, {'each rank its own B' if args.scaling == 'weak' and dist.world > 1 else 'one B split'} x{dist.world}; no collective on the hot path",
+            "l2": f"{sg.n_sets} rotating input/output sets, {sg.n_sets * sg.set_bytes / 2**20:.0f} MiB > L2 (126 MB); unflushed: one set",
+            "timing": f"one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks, median of {args.repeats} repeats of {args.steps} steps",
         },
+        "spread": spread(step_ms),
+        "unflushed": {"ms_per_step": statistics.median(unflushed_ms), "value": atoms_total / (statistics.median(unflushed_ms) * 1e-3), "spread": spread(unflushed_ms)},
         "roofline": roofline,
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,
-        "kernels": "block_forward_kernel + block_backward_xyz_kernel per step",
+        "kernels": "block_forward_kernel + block_backward_xyz_kernel per step (the vector-slot forms)",
         "clocks": sampler.summary(),
     }
+    if other is not None:
+        result[other["scaling"]] = other
     if allgather is not None:
         result["allgather"] = allgather
+    if ref_kernels is not None:
+        result["ref_kernels"] = ref_kernels
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(n)
     return result
+
+
+def time_reference_kernels(cufk, sg: "StepGraphs", n: int, stream, args) -> dict:
+    """The reference's own block kernels (its block.cu compiled from source into oracle/_ref by
+    oracle/build_ref.py) against cufk_b200 on the same rotating input sets, both through their
+    autograd path, eagerly (a forward, then backward of the step's grad): a measurement leg, like
+    cpu_baseline; the timed step above never touches oracle/."""
+    try:
+        from oracle import ref_kernels
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"oracle.ref_kernels: {exc}"}
+    if not ref_kernels.available("block"):
+        return {"unavailable": "oracle/_ref/block/cufk_ref_block.so not built"}
+    dev = sg.sets[0]["lengths"].device
+    anchors = {
+        "p0": torch.zeros(3, device=dev),
+        "first_direction": torch.tensor([1.0, 0.0, 0.0], device=dev),
+        "initial_normal": torch.tensor([0.0, 0.0, 1.0], device=dev),
+    }
+
+    def step(fn, d):
+        L, A, D = (d[k].detach().requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+        xyz = fn(L, A, D, **anchors)
+        xyz.backward(d["grad"])
+
+    out = {}
+    reps = min(args.steps, 200)
+    with torch.cuda.stream(stream):
+        for name, fn in (("reference", ref_kernels.ref_reconstruct), ("cufk_b200", cufk.reconstruct)):
+            for k in range(5):
+                step(fn, sg.sets[k % len(sg.sets)])
+            times = []
+            for _ in range(max(1, args.repeats)):
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for k in range(reps):
+                    step(fn, sg.sets[k % len(sg.sets)])
+                e1.record(stream)
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) / reps)
+            out[name] = {"ms_per_step": statistics.median(times), "spread": spread(times)}
+    ref_ms, our_ms = out["reference"]["ms_per_step"], out["cufk_b200"]["ms_per_step"]
+    return {
+        "reference_ms_per_step": ref_ms,
+        "cufk_b200_ms_per_step": our_ms,
+        "speedup": ref_ms / our_ms,
+        "reference_value": sg.b_local * n / (ref_ms * 1e-3),
+        "mode": "both through autograd, eager (forward + backward of a fixed grad per step), explicit default anchors, the same rotating input sets",
+        "detail": out,
+        "kernels": "reference: block_forward_kernel / block_backward_kernel of its block.cu built for sm_100a (oracle/_ref)",
+    }
 
 
 def gpu_local_cpus(device_index: int) -> set[int]:
@@ -464,6 +589,17 @@ def gpu_local_cpus(device_index: int) -> set[int]:
     return cpus & os.sched_getaffinity(0)
 
 
+def numa_node_of(cpus: set[int]) -> int:
+    """NUMA node of the first of `cpus` (from sysfs), -1 when unknown."""
+    for cpu in sorted(cpus)[:1]:
+        for entry in Path(f"/sys/devices/system/cpu/cpu{cpu}").glob("node*"):
+            try:
+                return int(entry.name[4:])
+            except ValueError:
+                pass
+    return -1
+
+
 def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     """Runs `_run_e2e` with the calling thread on the GPU's own NUMA node: the pinned host buffers
     are allocated (first touched) there, so the copies do not cross the socket interconnect.  The
@@ -477,6 +613,13 @@ def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     finally:
         os.sched_setaffinity(0, before)
     out["host_cpus"] = f"{len(local)} GPU-local cores (NVML affinity)" if local else "unchanged (no NVML affinity)"
+    node = numa_node_of(local if local else before)
+    ranks = dist.gather([node, out.pop("_h2d_gbs"), out.pop("_d2h_gbs")])
+    out["per_rank"] = [{"rank": r, "numa_node": int(v[0]), "h2d_gbs": round(v[1], 1), "d2h_gbs": round(v[2], 1)} for r, v in enumerate(ranks)]
+    out["ceiling_note"] = (
+        "each step moves h2d_bytes_per_step + d2h_bytes_per_step per rank over its PCIe link; the copy-only "
+        "rates above bound the e2e step at max(h2d / h2d_gbs, d2h / d2h_gbs) when the two directions overlap"
+    )
     return out
 
 
@@ -544,6 +687,34 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     # the results arrived: check them against a direct call
     ref = cufk.reconstruct(pinned["lengths"].to(dev), pinned["angles"].to(dev), pinned["dihedrals"].to(dev))
     assert torch.equal(outs["xyz"], ref.cpu()), "e2e output mismatch"
+    # copy-only rates of this rank's link, each direction alone (all ranks at once)
+    def copy_rate(direction):
+        reps = 10
+        with torch.cuda.stream(s_in):
+            for _ in range(2):
+                copy_once(direction)
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s_in)
+            for _ in range(reps):
+                copy_once(direction)
+            e1.record(s_in)
+            torch.cuda.synchronize()
+        nbytes = h2d if direction == "h2d" else d2h
+        return nbytes * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+
+    dev_out = {k: torch.empty_like(v, device=dev) for k, v in outs.items()}
+
+    def copy_once(direction):
+        if direction == "h2d":
+            for k in ("lengths", "angles", "dihedrals", "grad"):
+                buf[k].copy_(pinned[k], non_blocking=True)
+        else:
+            for k, v in outs.items():
+                v.copy_(dev_out[k], non_blocking=True)
+
+    h2d_gbs, d2h_gbs = copy_rate("h2d"), copy_rate("d2h")
     return {
         "value": global_batch * args.points / (ms * 1e-3),
         "unit": "atoms/s",
@@ -552,6 +723,8 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
         "ms_per_step": ms,
         "steps": steps,
         "path": "cufk_b200.reconstruct + autograd backward; pinned host buffers, copies inside the timed region; copy-in / compute / copy-out on three streams",
+        "_h2d_gbs": h2d_gbs,
+        "_d2h_gbs": d2h_gbs,
     }
 
 

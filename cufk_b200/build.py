@@ -31,7 +31,7 @@ EXT = PKG / "_C.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", *ARCH]
 CUDA_SOURCES = [CSRC / "cufkb_api.cu"]
-CUDA_DEPENDS = [CSRC / "nerf_device.cuh", CSRC / "nerf_kernels.cuh", CSRC / "nerf_long.cuh", CSRC / "nerf_math.cuh", INCLUDE / "cufkb.h"]
+CUDA_DEPENDS = [CSRC / "nerf_device.cuh", CSRC / "nerf_kernels.cuh", CSRC / "nerf_long.cuh", CSRC / "nerf_math.cuh", CSRC / "nerf_vec.cuh", INCLUDE / "cufkb.h"]
 EXT_SOURCES = [CSRC / "torch_ext.cpp"]
 
 

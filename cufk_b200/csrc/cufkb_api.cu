@@ -8,6 +8,7 @@
 #include "cufkb.h"
 #include "nerf_kernels.cuh"
 #include "nerf_long.cuh"
+#include "nerf_vec.cuh"
 
 #include <atomic>
 #include <cstdint>
@@ -21,7 +22,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 44;
+constexpr int kNumKernels = 88;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -262,13 +263,262 @@ enum KernelKind {
   kLongForward = 7,
   kLongSums = 8,
   kLongBackward = 9,
-  kBlockMse = 10
+  kBlockMse = 10,
+  // vector-slot kernels, one kind per (warps per chain, chains per CTA) instantiation
+  kVecForward1x1 = 11,
+  kVecForward1x2 = 12,
+  kVecForward1x4 = 13,
+  kVecForward2x1 = 14,
+  kVecForward4x1 = 15,
+  kVecForward8x1 = 16,
+  kVecBackward1 = 17,
+  kVecBackward2 = 18,
+  kVecBackward4 = 19,
+  kVecBackward8 = 20
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
+// ---------------------------------------------------------------------------------------------
+// vector-slot kernels (float32, float64): plan and launch
+// ---------------------------------------------------------------------------------------------
+// Warps per chain of the vector kernels; 0 lets the plan choose.  A chain's K atoms per thread are
+// a multiple of G = 16 / sizeof(T) and give an odd number of groups of G (three 16-byte shared
+// accesses per group then fall on distinct banks across each quarter warp).
+#ifndef CUFKB_VEC_FWD_WARPS
+#define CUFKB_VEC_FWD_WARPS 0
+#endif
+#ifndef CUFKB_VEC_BWD_WARPS
+#define CUFKB_VEC_BWD_WARPS 0
+#endif
+// Resident warps per SM the vector kernels' plans aim for (the forward is issue-bound and wants
+// many warps; the xyz backward's per-thread fixed work favours fewer, longer threads).
+#ifndef CUFKB_VEC_TARGET_WARPS
+#define CUFKB_VEC_TARGET_WARPS 32
+#endif
+#ifndef CUFKB_VEC_BWD_TARGET_WARPS
+#define CUFKB_VEC_BWD_TARGET_WARPS 20
+#endif
+#ifndef CUFKB_VEC_MAX_GROUPS
+#define CUFKB_VEC_MAX_GROUPS 7
+#endif
+
+struct VecPlan {
+  int warps;   // W
+  int chains;  // C (chains per CTA)
+  int items;   // K
+};
+
+// The largest shift of a thread range in the batch: known exactly when every chain's output row has
+// the residue mod 16 of the first one ((B, N) rows whose pitch is a multiple of 16 bytes).
+template <typename T>
+int vec_delta_max(const void* row0, int points, bool packed) {
+  const bool uniform = !packed && (size_t(3) * points * sizeof(T)) % 16 == 0;
+  return uniform ? cufkb::vec_delta<T>(reinterpret_cast<uintptr_t>(row0) & 15u) : cufkb::VecSlots<T>::kAtoms - 1;
+}
+
+// Items per thread for W warps: the fewest groups of G atoms that cover N + delta atoms with 32 W
+// threads, made odd.
+template <typename T>
+int vec_items(int points, int delta, int warps) {
+  constexpr int G = cufkb::VecSlots<T>::kAtoms;
+  int groups = ceil_div(points + delta, int64_t(cufkb::kWarp) * warps * G);
+  if ((groups & 1) == 0) ++groups;
+  return groups * G;
+}
+
+template <int W, int C>
+constexpr KernelKind vec_forward_kind() {
+  if constexpr (W == 1) return C == 1 ? kVecForward1x1 : (C == 2 ? kVecForward1x2 : kVecForward1x4);
+  return W == 2 ? kVecForward2x1 : (W == 4 ? kVecForward4x1 : kVecForward8x1);
+}
+
+// Resident CTAs per SM of a kernel instantiation with `smem` bytes of dynamic shared memory.
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int kind, int dtype_idx, size_t smem, int warps_per_cta, int* error) {
+  int dev = 0;
+  if (int e = current_device(&dev)) {
+    *error = e;
+    return 0;
+  }
+  const DeviceCache* d = device_cache(dev);
+  const KernelCache* k = kernel_cache(kernel, kernel_id(static_cast<KernelKind>(kind), dtype_idx));
+  if (d->error || k->error) {
+    *error = d->error ? d->error : k->error;
+    return 0;
+  }
+  return resident_warps(*d, *k, smem, warps_per_cta) / warps_per_cta;
+}
+
+template <typename T, int W, int C>
+int launch_vec_forward(const cufkb::BlockArgs<T>& args, T* xyz, int64_t batch, int points, int items, cudaStream_t stream, cufkb::PackedLayout packed) {
+  auto kernel = cufkb::block_forward_vec_kernel<T, W, C>;
+  const size_t smem = C * cufkb::vec_row_bytes(points, items, sizeof(T));
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(vec_forward_kind<W, C>(), dtype_index<T>()), batch, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
+  const unsigned grid = static_cast<unsigned>((batch + C - 1) / C);
+  kernel<<<grid, cufkb::kWarp * W * C, smem, stream>>>(args, xyz, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Warps per chain of the vector forward: the fewest with at most CUFKB_VEC_MAX_GROUPS groups of G
+// atoms per thread (an odd number of groups), then more while the SM would hold fewer than the
+// target of resident warps (shared memory bounds the chains of one warp), or while the grid offers
+// fewer than the target per SM (small batches), as long as the split leaves every warp busy.
+template <typename T>
+int vec_forward_warps(int64_t batch, int points, int delta) {
+  int w = 1;
+  while (w < cufkb::kMaxWarps && vec_items<T>(points, delta, w) / cufkb::VecSlots<T>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
+  if (CUFKB_VEC_FWD_WARPS > 0) return CUFKB_VEC_FWD_WARPS > w ? CUFKB_VEC_FWD_WARPS : w;
+  int dev = 0;
+  if (current_device(&dev)) return w;
+  const DeviceCache* d = device_cache(dev);
+  const int sms = d->error ? 148 : d->sm_count;
+  auto resident = [&](int warps) {
+    int err = 0, r = 0;
+    const size_t smem = cufkb::vec_row_bytes(points, vec_items<T>(points, delta, warps), sizeof(T));
+    switch (warps) {
+      case 1:
+        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 1, 1>, kVecForward1x1, dtype_index<T>(), smem, 1, &err);
+        break;
+      case 2:
+        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 2, 1>, kVecForward2x1, dtype_index<T>(), smem, 2, &err);
+        break;
+      case 4:
+        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 4, 1>, kVecForward4x1, dtype_index<T>(), smem, 4, &err);
+        break;
+      default:
+        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 8, 1>, kVecForward8x1, dtype_index<T>(), smem, 8, &err);
+        break;
+    }
+    return err ? 0 : r * warps;
+  };
+  // a split is worth it only while the next plan keeps at least half of its threads on atoms
+  auto busy = [&](int warps) {
+    const int items = vec_items<T>(points, delta, warps);
+    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
+  };
+  while (w < cufkb::kMaxWarps && busy(2 * w)) {
+    const bool low_residency = resident(w) < CUFKB_VEC_TARGET_WARPS && resident(2 * w) > resident(w);
+    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_TARGET_WARPS;
+    if (!(low_residency || small_grid)) break;
+    w *= 2;
+  }
+  return w;
+}
+
+template <typename T>
+int block_forward_vec(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
+                      cudaStream_t stream, cufkb::PackedLayout packed) {
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const int delta = vec_delta_max<T>(xyz, points, packed.offsets != nullptr);
+  const int w = vec_forward_warps<T>(batch, points, delta);
+  const int items = vec_items<T>(points, delta, w);
+  T* out = static_cast<T*>(xyz);
+  switch (w) {
+    case 1:
+      return launch_vec_forward<T, 1, 1>(args, out, batch, points, items, stream, packed);
+    case 2:
+      return launch_vec_forward<T, 2, 1>(args, out, batch, points, items, stream, packed);
+    case 4:
+      return launch_vec_forward<T, 4, 1>(args, out, batch, points, items, stream, packed);
+    default:
+      return launch_vec_forward<T, 8, 1>(args, out, batch, points, items, stream, packed);
+  }
+}
+
+// Resident warps per SM of a kernel instantiation with `smem` bytes of dynamic shared memory.
+template <typename Kernel>
+int vec_resident_warps(Kernel kernel, int kind, int dtype_idx, size_t smem, int warps_per_cta, int* error) {
+  return resident_ctas(kernel, kind, dtype_idx, smem, warps_per_cta, error) * warps_per_cta;
+}
+
+template <typename T, int W>
+int launch_vec_backward(const cufkb::BlockArgs<T>& args, const T* xyz, const T* g, T* gL, T* gA, T* gD, int64_t batch, int points, int items,
+                        cudaStream_t stream, cufkb::PackedLayout packed_layout) {
+  auto kernel = cufkb::block_backward_xyz_vec_kernel<T, W>;
+  const size_t smem = 2 * cufkb::vec_row_bytes(points, items, sizeof(T));
+  constexpr KernelKind kind = W == 1 ? kVecBackward1 : (W == 2 ? kVecBackward2 : (W == 4 ? kVecBackward4 : kVecBackward8));
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(kind, dtype_index<T>()), batch, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed_layout};
+  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args, xyz, g, gL, gA, gD, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Warps per chain of the vector xyz backward: as vec_forward_warps, on its own footprint.
+template <typename T>
+int vec_backward_warps(int64_t batch, int points, int delta) {
+  if (CUFKB_VEC_BWD_WARPS > 0) return CUFKB_VEC_BWD_WARPS;
+  int dev = 0;
+  if (current_device(&dev)) return 2;
+  const DeviceCache* d = device_cache(dev);
+  const int sms = d->error ? 148 : d->sm_count;
+  int w = 1;
+  while (w < cufkb::kMaxWarps && vec_items<T>(points, delta, w) / cufkb::VecSlots<T>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
+  auto resident = [&](int warps) {
+    int err = 0;
+    const size_t smem = 2 * cufkb::vec_row_bytes(points, vec_items<T>(points, delta, warps), sizeof(T));
+    int r = 0;
+    switch (warps) {
+      case 1:
+        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 1>, kVecBackward1, dtype_index<T>(), smem, 1, &err);
+        break;
+      case 2:
+        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 2>, kVecBackward2, dtype_index<T>(), smem, 2, &err);
+        break;
+      case 4:
+        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 4>, kVecBackward4, dtype_index<T>(), smem, 4, &err);
+        break;
+      default:
+        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 8>, kVecBackward8, dtype_index<T>(), smem, 8, &err);
+        break;
+    }
+    return err ? 0 : r;
+  };
+  auto busy = [&](int warps) {
+    const int items = vec_items<T>(points, delta, warps);
+    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
+  };
+  while (w < cufkb::kMaxWarps && busy(2 * w)) {
+    const bool low_residency = resident(w) < CUFKB_VEC_BWD_TARGET_WARPS && resident(2 * w) > resident(w);
+    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_BWD_TARGET_WARPS;
+    if (!(low_residency || small_grid)) break;
+    w *= 2;
+  }
+  return w;
+}
+
+template <typename T>
+int block_backward_xyz_vec(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
+                           void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed_layout) {
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const int delta = vec_delta_max<T>(xyz, points, packed_layout.offsets != nullptr);
+  const int w = vec_backward_warps<T>(batch, points, delta);
+  const int items = vec_items<T>(points, delta, w);
+  const T* x = static_cast<const T*>(xyz);
+  const T* gg = static_cast<const T*>(g);
+  T *l = static_cast<T*>(gL), *a = static_cast<T*>(gA), *d = static_cast<T*>(gD);
+  switch (w) {
+    case 1:
+      return launch_vec_backward<T, 1>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
+    case 2:
+      return launch_vec_backward<T, 2>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
+    case 4:
+      return launch_vec_backward<T, 4>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
+    default:
+      return launch_vec_backward<T, 8>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
+  }
+}
+
 template <typename T>
 int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
-                       cudaStream_t stream, const int64_t* offsets = nullptr) {
+                       cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
+  if constexpr (sizeof(T) >= 4) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
@@ -277,7 +527,7 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   }
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
@@ -285,14 +535,14 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
 
 template <typename T>
 int block_backward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* g, void* gL, void* gA,
-                        void* gD, int64_t batch, int points, cudaStream_t stream, const int64_t* offsets = nullptr) {
+                        void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kBlockBackward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTargetWarpsPerSm))) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
                                                                           static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
@@ -302,14 +552,18 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
 // Backward from the forward's xyz (32- and 64-bit types).
 template <typename T>
 int block_backward_xyz_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
-                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, const int64_t* offsets = nullptr) {
+                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
+  // the vector kernel stages xyz and grad rows with one shift: their rows must share the residue mod 16
+  if ((reinterpret_cast<uintptr_t>(xyz) - reinterpret_cast<uintptr_t>(g)) % 16 == 0) {
+    return block_backward_xyz_vec<T>(L, A, D, p0, fd, nn, xyz, g, gL, gA, gD, batch, points, stream, packed_layout);
+  }
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
   auto kernel = cufkb::block_backward_xyz_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kBlockBackwardXyz, dtype_index<T>()), batch, points, smem, kXyzTargetWarpsPerSm)) return st;
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, offsets};
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
                                                                           static_cast<T*>(gA), static_cast<T*>(gD), geo);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
@@ -421,12 +675,22 @@ int long_totals_launch(const cufkb::BlockArgs<T>& args, typename cufkb::ComputeO
   return CUFKB_SUCCESS;
 }
 
+// Turns the segment totals (and sums) into carries (and suffixes): one thread per chain.
+template <typename R>
+int long_scan_launch(R* totals, R* sums, int64_t batch, const LongPlan& lp, cudaStream_t stream) {
+  constexpr int kThreads = 128;
+  cufkb::long_scan_kernel<R><<<ceil_div(batch, kThreads), kThreads, 0, stream>>>(totals, sums, static_cast<int>(batch), lp.segs);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
 template <typename T>
 int block_forward_long_impl(const cufkb::BlockArgs<T>& args, void* xyz, int64_t batch, int64_t points, void* workspace, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
   const LongPlan lp = long_plan(points);
   R* totals = static_cast<R*>(workspace);
   if (int st = long_totals_launch<T>(args, totals, batch, points, lp, stream)) return st;
+  if (int st = long_scan_launch<R>(totals, nullptr, batch, lp, stream)) return st;
   const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, false);
   auto kernel = cufkb::long_forward_kernel<T>;
   LaunchEnv env;
@@ -453,6 +717,7 @@ int block_backward_long_impl(const cufkb::BlockArgs<T>& args, const void* xyz, c
     kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, 0, stream>>>(static_cast<const T*>(xyz), static_cast<const T*>(g), sums, geo);
     if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   }
+  if (int st = long_scan_launch<R>(totals, sums, batch, lp, stream)) return st;
   const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, true);
   auto kernel = cufkb::long_backward_kernel<T>;
   LaunchEnv env;
@@ -482,21 +747,27 @@ constexpr size_t kStaticScratchBytes = size_t(2) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 struct ScratchAddress {
-  std::once_flag once;
-  void* ptr = nullptr;
-  int error = 0;
+  std::mutex lock;
+  std::atomic<void*> ptr{nullptr};
 };
 ScratchAddress g_scratch_address[kMaxDevices];
 
-// The array's address on device `dev`, looked up once per device.
+// The array's address on device `dev` (the current device), looked up on the first call that
+// succeeds there and cached from then on; a failed lookup is returned and retried by the next call.
 void* static_scratch(int dev, int* error) {
   ScratchAddress& a = g_scratch_address[dev];
-  std::call_once(a.once, [&] {
-    const cudaError_t e = cudaGetSymbolAddress(&a.ptr, g_static_scratch);
-    a.error = static_cast<int>(e);
-  });
-  *error = a.error;
-  return a.ptr;
+  *error = 0;
+  if (void* p = a.ptr.load(std::memory_order_acquire)) return p;
+  std::lock_guard<std::mutex> guard(a.lock);
+  if (void* p = a.ptr.load(std::memory_order_relaxed)) return p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) {
+    *error = static_cast<int>(e);
+    return nullptr;
+  }
+  a.ptr.store(p, std::memory_order_release);
+  return p;
 }
 
 }  // namespace
@@ -522,28 +793,28 @@ int check_offsets(const int64_t* offsets, bool packed) {
 }
 
 int block_forward_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch,
-                           int64_t points, cufkb_stream_t stream, bool packed = false, const int64_t* offsets = nullptr) {
+                           int64_t points, cufkb_stream_t stream, bool packed = false, cufkb::PackedLayout packed_layout = {}) {
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
   if (int st = check_block_pointers(dtype, {L, A, D, xyz}, {L, A, D, p0, fd, nn, xyz})) return st;
-  if (int st = check_offsets(offsets, packed)) return st;
+  if (int st = check_offsets(packed_layout.offsets, packed)) return st;
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
-      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
+      return block_forward_impl<float>(L, A, D, p0, fd, nn, xyz, batch, n, s, packed_layout);
     case CUFKB_FLOAT64:
-      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
+      return block_forward_impl<double>(L, A, D, p0, fd, nn, xyz, batch, n, s, packed_layout);
     case CUFKB_FLOAT16:
-      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
+      return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s, packed_layout);
     default:
-      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s, offsets);
+      return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s, packed_layout);
   }
 }
 
 int block_backward_dispatch(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                             const void* initial_normal, const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
-                            int64_t points, cufkb_stream_t stream, bool packed = false, const int64_t* offsets = nullptr) {
+                            int64_t points, cufkb_stream_t stream, bool packed = false, cufkb::PackedLayout packed_layout = {}) {
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
   if (int st = check_block_pointers(dtype, {lengths, angles, dihedrals, grad_xyz, grad_lengths, grad_angles, grad_dihedrals},
@@ -551,34 +822,34 @@ int block_backward_dispatch(int dtype, const void* lengths, const void* angles, 
                                      grad_dihedrals})) {
     return st;
   }
-  if (int st = check_offsets(offsets, packed)) return st;
+  if (int st = check_offsets(packed_layout.offsets, packed)) return st;
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CUFKB_FLOAT32:
       return block_backward_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                        grad_dihedrals, batch, n, s, offsets);
+                                        grad_dihedrals, batch, n, s, packed_layout);
     case CUFKB_FLOAT64:
       return block_backward_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s, offsets);
+                                         grad_dihedrals, batch, n, s, packed_layout);
     case CUFKB_FLOAT16:
       return block_backward_impl<__half>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s, offsets);
+                                         grad_dihedrals, batch, n, s, packed_layout);
     default:
       return block_backward_impl<__nv_bfloat16>(lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                                grad_dihedrals, batch, n, s, offsets);
+                                                grad_dihedrals, batch, n, s, packed_layout);
   }
 }
 
 int block_backward_from_xyz_dispatch(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                                      const void* initial_normal, const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
                                      void* grad_dihedrals, int64_t batch, int64_t points, cufkb_stream_t stream, bool packed = false,
-                                     const int64_t* offsets = nullptr) {
+                                     cufkb::PackedLayout packed_layout = {}) {
   if (dtype != CUFKB_FLOAT32 && dtype != CUFKB_FLOAT64) {
     if (int st = check_shape(dtype, batch, points)) return st;
     if (batch > 0 && !xyz) return CUFKB_ERROR_NULL_POINTER;
     return block_backward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, grad_xyz, grad_lengths, grad_angles,
-                                   grad_dihedrals, batch, points, stream, packed, offsets);
+                                   grad_dihedrals, batch, points, stream, packed, packed_layout);
   }
   if (int st = check_shape(dtype, batch, points)) return st;
   if (batch == 0) return CUFKB_SUCCESS;
@@ -587,15 +858,15 @@ int block_backward_from_xyz_dispatch(int dtype, const void* lengths, const void*
                                      grad_dihedrals})) {
     return st;
   }
-  if (int st = check_offsets(offsets, packed)) return st;
+  if (int st = check_offsets(packed_layout.offsets, packed)) return st;
   const int n = static_cast<int>(points);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == CUFKB_FLOAT32) {
     return block_backward_xyz_impl<float>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
-                                          grad_dihedrals, batch, n, s, offsets);
+                                          grad_dihedrals, batch, n, s, packed_layout);
   }
   return block_backward_xyz_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths, grad_angles,
-                                         grad_dihedrals, batch, n, s, offsets);
+                                         grad_dihedrals, batch, n, s, packed_layout);
 }
 
 }  // namespace
@@ -646,19 +917,27 @@ int cufkb_block_mse(int dtype, const void* lengths, const void* angles, const vo
                                 batch, n, s);
 }
 
+// The packed total (points of all chains) must be >= 4 B; offsets outside it only skip chains.
+int check_packed_total(int64_t batch, int64_t total_points) {
+  return (total_points < 0 || (batch > 0 && total_points < 4 * batch)) ? CUFKB_ERROR_SHAPE_LIMITS : CUFKB_SUCCESS;
+}
+
 int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
-                               const void* initial_normal, const int64_t* chain_points, void* xyz, int64_t batch, int64_t max_points,
-                               cufkb_stream_t stream) {
+                               const void* initial_normal, const int64_t* chain_points, void* xyz, int64_t batch, int64_t total_points,
+                               int64_t max_points, cufkb_stream_t stream) {
+  if (int st = check_packed_total(batch, total_points)) return st;
   return block_forward_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, batch, max_points, stream, true,
-                                chain_points);
+                                cufkb::PackedLayout{chain_points, total_points});
 }
 
 int cufkb_block_backward_packed_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                                          const void* first_direction, const void* initial_normal, const int64_t* chain_points, const void* xyz,
                                          const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
-                                         int64_t max_points, cufkb_stream_t stream) {
+                                         int64_t total_points, int64_t max_points, cufkb_stream_t stream) {
+  if (int st = check_packed_total(batch, total_points)) return st;
   return block_backward_from_xyz_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz, grad_lengths,
-                                          grad_angles, grad_dihedrals, batch, max_points, stream, true, chain_points);
+                                          grad_angles, grad_dihedrals, batch, max_points, stream, true,
+                                          cufkb::PackedLayout{chain_points, total_points});
 }
 
 int cufkb_torsion_forward(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,

@@ -164,6 +164,12 @@ __device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {
 }
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+// Waits until at most `Pending` of this thread's committed cp.async groups are still in flight.
+template <int Pending>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(Pending) : "memory");
+}
 
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -523,14 +529,19 @@ __device__ __forceinline__ ChainFrame<V> chain_frame(const AnchorFrame<typename 
 // ------------------------------------------------------------------------------------------
 // launch geometry shared by host and device
 // ------------------------------------------------------------------------------------------
+// A packed (ragged) batch: chain b's points are [offsets[b], offsets[b+1]) of the packed xyz of
+// `total` points; offsets is null for a (B, N) batch.
+struct PackedLayout {
+  const int64_t* offsets = nullptr;
+  int64_t total = 0;
+};
+
 struct ChainGeometry {
   int batch;   // B
   int points;  // N (a packed batch: the largest N of its chains)
   int steps;   // N - 3
-  int items;   // K: steps per thread (odd)
-  // Packed (ragged) batch: chain b's points are [offsets[b], offsets[b+1]) of the packed xyz; null
-  // for a (B, N) batch.
-  const int64_t* offsets = nullptr;
+  int items;   // K: steps per thread
+  PackedLayout packed = {};
 };
 
 // Element offsets of one chain's rows in the (B, N-1), (B, N-2), (B, N-3) and (B, N, 3) arrays,
@@ -545,13 +556,19 @@ __host__ __device__ inline ChainRows rows_at(int64_t chain, int64_t first_point,
   return {points, first_point - chain, first_point - 2 * chain, first_point - 3 * chain, 3 * first_point};
 }
 
-// A packed chain whose point count lies outside [4, geo.points] gets points = 0 (the kernels leave
-// it untouched).
+// A packed chain gets points = 0 (the kernels leave it untouched) when its point count lies outside
+// [4, geo.points] or when any of its four rows would reach outside its packed array: xyz
+// [p, p + n) in [0, total), lengths [p - b, p - b + n - 1) in [0, total - B), angles
+// [p - 2b, ...) in [0, total - 2B), dihedrals [p - 3b, ...) in [0, total - 3B).  So offsets that
+// are not those of a packed layout cannot make a kernel read or write out of bounds.
 __device__ __forceinline__ ChainRows chain_rows(const ChainGeometry& g, int64_t chain) {
-  if (g.offsets == nullptr) return rows_at(chain, chain * g.points, g.points);
-  const int64_t p0 = g.offsets[chain];
-  const int64_t n = g.offsets[chain + 1] - p0;
-  return rows_at(chain, p0, (n >= 4 && n <= g.points) ? static_cast<int>(n) : 0);
+  if (g.packed.offsets == nullptr) return rows_at(chain, chain * g.points, g.points);
+  const int64_t p0 = g.packed.offsets[chain];
+  const int64_t n = g.packed.offsets[chain + 1] - p0;
+  const int64_t B = g.batch, total = g.packed.total;
+  const bool inside = n >= 4 && n <= g.points && p0 - 3 * chain >= 0 && p0 + n <= total && p0 - chain + n - 1 <= total - B &&
+                      p0 - 2 * chain + n - 2 <= total - 2 * B && p0 - 3 * chain + n - 3 <= total - 3 * B;
+  return rows_at(chain, inside ? p0 : 0, inside ? static_cast<int>(n) : 0);
 }
 
 }  // namespace cufkb

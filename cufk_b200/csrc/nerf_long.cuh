@@ -6,13 +6,18 @@
 // workspace in global memory (no CTA waits for another: every exchange is between two launches):
 //
 //   forward   long_totals_kernel    T_g = product of segment g's local transforms  -> totals[g]
-//             long_forward_kernel   world carry (F, p2) T_0 ... T_{g-1} (thread 0, sequential
-//                                   compose), then the one-CTA forward of the segment from it
+//             long_scan_kernel      totals[g] <- T_0 ... T_{g-1} (one thread per chain, in place)
+//             long_forward_kernel   world carry (F, p2) totals[g], then the one-CTA forward of the
+//                                   segment from it
 //   backward  long_totals_kernel    as above (the carries)
 //             long_sums_kernel      G_g = sum g_j, M_g = sum x_j x g_j over segment g's atoms, from
 //                                   the forward's xyz                              -> sums[g]
+//             long_scan_kernel      totals as above, and sums[g] <- the sums of all later segments
 //             long_backward_kernel  the one-CTA recompute backward of the segment (world
 //                                   coordinates) from its carry and the sums of all later segments
+//
+// The scan between the launches keeps the work linear in the number of segments: every CTA reads
+// one carry and one suffix instead of combining all the segments in front of (or behind) its own.
 //
 // Segment g covers steps [g L, min(S, (g + 1) L)), L = ceil(S / segs), and writes the atoms of its
 // steps (s + 3); segment 0 also writes atoms 0..2 and the first-frame gradients.  Inside a
@@ -86,12 +91,31 @@ __device__ __forceinline__ Affine<V> load_total(const R* src) {
   return a;
 }
 
-// (F, p2) T_0 ... T_{g-1}: the world frame in front of segment g (one thread).
-template <typename V, typename R>
-__device__ __forceinline__ Affine<V> segment_carry(const R* chain_totals, int g, const V* F, const V* p2) {
-  Affine<V> C = affine_identity<V>();
-  for (int j = 0; j < g; ++j) C = compose(C, load_total<V>(chain_totals + j * kTotalWords));
-  return world_carry(C, F, p2);
+// Exclusive prefix of every chain's segment totals, in place: totals[g] <- T_0 ... T_{g-1} (the
+// identity for g = 0), composed left to right.  With sums non-null, also the exclusive suffix of the
+// segment sums: sums[g] <- the sum over the segments after g.  One thread per chain.
+template <typename R>
+__global__ void long_scan_kernel(R* __restrict__ totals, R* __restrict__ sums, int batch, int segs) {
+  const int64_t chain = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (chain >= batch) return;
+  R* t = totals + chain * segs * kTotalWords;
+  Affine<R> C = affine_identity<R>();
+  for (int g = 0; g < segs; ++g) {
+    const Affine<R> T = load_total<R>(t + int64_t(g) * kTotalWords);
+    store_total(t + int64_t(g) * kTotalWords, C);
+    C = compose(C, T);
+  }
+  if (sums == nullptr) return;
+  R* sm = sums + chain * segs * kSumWords;
+  R acc[kSumWords] = {R(0), R(0), R(0), R(0), R(0), R(0)};
+  for (int g = segs - 1; g >= 0; --g) {
+#pragma unroll
+    for (int i = 0; i < kSumWords; ++i) {
+      const R v = sm[int64_t(g) * kSumWords + i];
+      sm[int64_t(g) * kSumWords + i] = acc[i];
+      acc[i] = acc[i] + v;
+    }
+  }
 }
 
 // T_g for every (chain, segment).
@@ -134,7 +158,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const SegmentOf sg = segment_of(geo);
   // segment 0 stores atoms 0 .. count+2 from slot 0; later segments atoms first+3 .. from slot 9
   const int first_slot = sg.g == 0 ? 0 : 9;
-  T* dst = xyz + sg.chain * 3 * N + (sg.g == 0 ? 0 : 3 * (sg.first + 3));
+  T* dst = xyz + sg.chain * 3 * N + (sg.g == 0 ? 0 : 3 * int64_t(sg.first + 3));
   const uintptr_t residue = (reinterpret_cast<uintptr_t>(dst) - first_slot * sizeof(T)) & 15u;
   ChainViews<T> cv;
   stage_segment_inputs<T>(cv, smem, args, sg, N, residue, tid, nthr);
@@ -142,7 +166,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   if (tid == 0) {
     const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
     const ChainFrame<V> ff = chain_frame_of<T, V>(args, af, rows_at(sg.chain, sg.chain * N, N));
-    const Affine<V> W = segment_carry<V>(totals + sg.chain * geo.segs * kTotalWords, sg.g, ff.F, ff.p2);
+    const Affine<V> W = world_carry(load_total<V>(totals + (sg.chain * geo.segs + sg.g) * kTotalWords), ff.F, ff.p2);
 #pragma unroll
     for (int i = 0; i < 9; ++i) ex.frame[i] = W.m[i];
 #pragma unroll
@@ -188,7 +212,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const T* x = xyz + sg.chain * 3 * N;
   const T* gr = grad_xyz + sg.chain * 3 * N;
   V acc[kSumWords] = {V(0), V(0), V(0), V(0), V(0), V(0)};
-  for (int a = sg.first + 3 + tid; a < sg.first + 3 + sg.count; a += nthr) {
+  for (int64_t a = sg.first + 3 + tid; a < int64_t(sg.first) + 3 + sg.count; a += nthr) {
     const V p[3] = {to_r<V>(x[3 * a]), to_r<V>(x[3 * a + 1]), to_r<V>(x[3 * a + 2])};
     const V g[3] = {to_r<V>(gr[3 * a]), to_r<V>(gr[3 * a + 1]), to_r<V>(gr[3 * a + 2])};
     V m[3];
@@ -238,26 +262,21 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   ChainViews<T> cv;
   stage_segment_inputs<T>(cv, smem, args, sg, N, 0, tid, nthr);
   // the grad row of the segment's atoms first .. first+count+2, in the local numbering of the slots
-  cv.G = stage_row_async(smem + slot_bytes(sg.count + 3, sizeof(R)), grow + 3 * sg.first, 3 * (sg.count + 3), tid, nthr);
+  cv.G = stage_row_async(smem + slot_bytes(sg.count + 3, sizeof(R)), grow + 3 * int64_t(sg.first), 3 * (sg.count + 3), tid, nthr);
   if (tid == 0) {
     const AnchorFrame<R> af = anchor_frame<R>(args.p0, args.first_direction, args.initial_normal);
     const R l0 = args.lengths[sg.chain * (N - 1)];
     const R l1 = args.lengths[sg.chain * (N - 1) + 1];
     const R a0 = args.angles[sg.chain * (N - 2)];
     first = FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0)};
-    const Affine<V> W = segment_carry<V>(totals + sg.chain * geo.segs * kTotalWords, sg.g, first.bf.ff.F, first.bf.ff.p2);
+    const Affine<V> W = world_carry(load_total<V>(totals + (sg.chain * geo.segs + sg.g) * kTotalWords), first.bf.ff.F, first.bf.ff.p2);
 #pragma unroll
     for (int i = 0; i < 9; ++i) ex.frame[i] = W.m[i];
 #pragma unroll
     for (int i = 0; i < 3; ++i) ex.frame[9 + i] = W.v[i];
-    V t[kSumWords] = {V(0), V(0), V(0), V(0), V(0), V(0)};
-    const R* cs = sums + sg.chain * geo.segs * kSumWords;
-    for (int j = sg.g + 1; j < geo.segs; ++j) {
+    const R* cs = sums + (sg.chain * geo.segs + sg.g) * kSumWords;
 #pragma unroll
-      for (int i = 0; i < kSumWords; ++i) t[i] = vadd(t[i], cs[j * kSumWords + i]);
-    }
-#pragma unroll
-    for (int i = 0; i < kSumWords; ++i) later[i] = t[i];
+    for (int i = 0; i < kSumWords; ++i) later[i] = cs[i];
   }
   cp_async_wait_all();
   __syncthreads();

@@ -314,6 +314,7 @@ PackedShape check_packed(const Tensor& lengths, const Tensor& angles, const Tens
   TORCH_CHECK(angles.size(0) == total - 2 * batch, "bad angles shape");
   TORCH_CHECK(dihedrals.size(0) == total - 3 * batch, "bad dihedrals shape");
   TORCH_CHECK(batch <= INT32_MAX, "shape exceeds int32 kernel limits");
+  TORCH_CHECK(total >= 4 * batch, "packed chains must hold at least 4 points each on average");
   TORCH_CHECK(batch == 0 || max_points >= 4, "point_count must be >= 4");
   TORCH_CHECK(max_points - 3 <= kMaxSteps, "reconstruct supports at most ", kMaxSteps, " local transforms");
   return {batch, total, max_points};
@@ -325,7 +326,7 @@ Tensor packed_forward_impl(const Tensor& lengths, const Tensor& angles, const Te
   Tensor xyz = torch::empty({shape.total, 3}, lengths.options());
   check_status(cufkb_block_forward_packed(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                           ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
-                                          chain_points.data_ptr<int64_t>(), xyz.data_ptr(), shape.batch, shape.max_points, current_stream()),
+                                          chain_points.data_ptr<int64_t>(), xyz.data_ptr(), shape.batch, shape.total, shape.max_points, current_stream()),
                "reconstruct_packed");
   return xyz;
 }
@@ -339,7 +340,7 @@ std::vector<Tensor> packed_backward_impl(const Tensor& lengths, const Tensor& an
   check_status(cufkb_block_backward_packed_from_xyz(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                                     ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
                                                     chain_points.data_ptr<int64_t>(), xyz.data_ptr(), grad_points.data_ptr(), gl.data_ptr(),
-                                                    ga.data_ptr(), gd.data_ptr(), shape.batch, shape.max_points, current_stream()),
+                                                    ga.data_ptr(), gd.data_ptr(), shape.batch, shape.total, shape.max_points, current_stream()),
                "reconstruct_packed backward");
   return {gl, ga, gd};
 }

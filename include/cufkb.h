@@ -124,20 +124,24 @@ CUFKB_API int cufkb_block_mse(int dtype, const void* lengths, const void* angles
  * [chain_points[b], chain_points[b+1]) of the packed xyz (total_points, 3), and its rows sit packed
  * the same way in lengths (total_points - B), angles (total_points - 2B) and dihedrals
  * (total_points - 3B): chain b's lengths start at chain_points[b] - b, its angles at
- * chain_points[b] - 2b, its dihedrals at chain_points[b] - 3b.  max_points is the largest chain
- * (4 <= max_points <= 2051); the launch is planned for it.  A chain whose point count lies outside
- * [4, max_points] is skipped: its outputs are left as they were.  The offsets stay on the device
- * (nothing is read back), so these calls validate only what the host knows.  Anchors and dtypes as
+ * chain_points[b] - 2b, its dihedrals at chain_points[b] - 3b.  total_points is the packed xyz's
+ * point count (at least 4 B) and fixes the sizes of the four packed arrays.  max_points is the
+ * largest chain (4 <= max_points <= 2051); the launch is planned for it.  A chain whose point
+ * count lies outside [4, max_points], or any of whose four rows would reach outside its packed
+ * array (negative or too large offsets), is skipped: its outputs are left as they were.  The
+ * offsets stay on the device (nothing is read back), so these calls validate only what the host
+ * knows; the kernels check every chain's rows against the packed sizes.  Anchors and dtypes as
  * for the (B, N) entry points; the backward reads the forward's xyz as
  * cufkb_block_backward_from_xyz does. */
 CUFKB_API int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                                const void* first_direction, const void* initial_normal, const int64_t* chain_points, void* xyz,
-                               int64_t batch, int64_t max_points, cufkb_stream_t stream);
+                               int64_t batch, int64_t total_points, int64_t max_points, cufkb_stream_t stream);
 
 CUFKB_API int cufkb_block_backward_packed_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                                          const void* first_direction, const void* initial_normal, const int64_t* chain_points,
                                          const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
-                                         void* grad_dihedrals, int64_t batch, int64_t max_points, cufkb_stream_t stream);
+                                         void* grad_dihedrals, int64_t batch, int64_t total_points, int64_t max_points,
+                                         cufkb_stream_t stream);
 
 /* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
  * elements (any stride >= 0, pairs within a row contiguous). */
@@ -181,10 +185,13 @@ CUFKB_API int cufkb_block_forward_long(int dtype, const void* lengths, const voi
  * (a loop with a fixed device-memory budget).
  *
  * The call allocates nothing.  Its scratch is a file-scope static device array of 2 MiB inside
- * libcufkb.so; the library looks up its address once per device, with cudaGetSymbolAddress, on the
- * first call on that device.  Make that first call outside any stream capture (a plain warm-up
- * call will do).  Nothing in the scratch needs to start at zero: each call writes the segment
- * totals before reading them.
+ * libcufkb.so; the library looks up its address with cudaGetSymbolAddress on the first call on a
+ * device and keeps it for later calls there.  Make that first call outside any stream capture (a
+ * plain warm-up call will do); a lookup that fails is returned as CUFKB_ERROR_CUDA and tried again
+ * by the next call.  The cached address belongs to the device's current context: after
+ * cudaDeviceReset on a device, this entry point must not be called again in that process.
+ * Nothing in the scratch needs to start at zero: each call writes the segment totals before
+ * reading them.
  *
  * Limits:
  * - batch x segments x 12 x sizeof(element) must fit in 2 MiB, where

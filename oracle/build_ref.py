@@ -106,13 +106,25 @@ def build(reference: Path, force: bool = False, which: str = "all") -> None:
         )
 
 
+def reference_checkout() -> Path | None:
+    """The cufk checkout to compile: $CUFKB_REFERENCE when set, else a directory named "reference"
+    beside this repository; None when neither exists."""
+    env = os.environ.get("CUFKB_REFERENCE")
+    candidate = Path(env) if env else Path(__file__).resolve().parent.parent.parent / "reference"
+    return candidate if candidate.is_dir() else None
+
+
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default=os.environ.get("CUFKB_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=None, help="cufk checkout (default: $CUFKB_REFERENCE, else ../reference)")
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--which", choices=["all", "block", "torsion"], default="all")
     args = ap.parse_args(argv)
-    build(Path(args.reference), force=args.force, which=args.which)
+    ref = Path(args.reference) if args.reference else reference_checkout()
+    if ref is None:
+        print("no reference checkout: set CUFKB_REFERENCE")
+        return 1
+    build(ref, force=args.force, which=args.which)
     return 0
 
 

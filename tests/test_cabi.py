@@ -154,22 +154,25 @@ def test_status_strings(lib):
 
 def test_packed_entry_points_validation(lib):
     vp, i64 = ctypes.c_void_p, ctypes.c_int64
-    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
-    lib.cufkb_block_backward_packed_from_xyz.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
+    lib.cufkb_block_backward_packed_from_xyz.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
 
-    def fwd_packed(offsets=128, batch=2, max_points=10, dtype=F32):
-        return lib.cufkb_block_forward_packed(dtype, 16, 32, 48, None, None, None, offsets, 64, batch, max_points, None)
+    def fwd_packed(offsets=128, batch=2, max_points=10, dtype=F32, total=20):
+        return lib.cufkb_block_forward_packed(dtype, 16, 32, 48, None, None, None, offsets, 64, batch, total, max_points, None)
 
     assert fwd_packed(offsets=None) == NULL_POINTER
     assert fwd_packed(offsets=132) == MISALIGNED  # int64 offsets need 8-byte alignment
     assert fwd_packed(max_points=3) == POINT_COUNT
     assert fwd_packed(max_points=2052) == TOO_MANY_STEPS
     assert fwd_packed(dtype=7) == INVALID_DTYPE
-    assert fwd_packed(batch=0, offsets=None) == SUCCESS  # nothing to launch
+    assert fwd_packed(batch=0, offsets=None, total=0) == SUCCESS  # nothing to launch
+    assert fwd_packed(total=7) == SHAPE_LIMITS  # fewer than 4 points per chain
+    assert fwd_packed(total=-1) == SHAPE_LIMITS
     bwd = lib.cufkb_block_backward_packed_from_xyz
-    assert bwd(F32, 16, 32, 48, None, None, None, None, 64, 80, 96, 112, 128, 2, 10, None) == NULL_POINTER
-    assert bwd(F32, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 2, 2052, None) == TOO_MANY_STEPS
-    assert bwd(F16, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 0, 10, None) == SUCCESS
+    assert bwd(F32, 16, 32, 48, None, None, None, None, 64, 80, 96, 112, 128, 2, 20, 10, None) == NULL_POINTER
+    assert bwd(F32, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 2, 20, 2052, None) == TOO_MANY_STEPS
+    assert bwd(F32, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 2, 7, 10, None) == SHAPE_LIMITS
+    assert bwd(F16, 16, 32, 48, None, None, None, 136, 64, 80, 96, 112, 128, 0, 0, 10, None) == SUCCESS
 
 
 def test_fused_mse_entry_point_validation(lib):

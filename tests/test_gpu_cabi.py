@@ -74,5 +74,7 @@ def test_unaligned_row_starts_through_cabi(lib):
         base = torch.full((7 * N * 3 + 1,), float("nan"), device="cuda")
         xyz = base[1:].view(7, N, 3)  # 4-byte aligned, not 16
         assert lib.cufkb_block_forward(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, xyz.data_ptr(), 7, N, torch.cuda.current_stream().cuda_stream) == 0
-        torch.testing.assert_close(xyz, _native._C.block_forward(L, A, D, None, None, None), rtol=0, atol=0)
+        # the threads' ranges follow the row's residue mod 16, so the scan's rounding may differ in
+        # the last bits from the aligned call
+        torch.testing.assert_close(xyz, _native._C.block_forward(L, A, D, None, None, None), rtol=0, atol=2e-6)
         assert torch.isnan(base[0])  # nothing written before the output

@@ -55,7 +55,9 @@ def test_short_chains_agree_with_one_cta_path(points):
     inp = nerf64.make_inputs(5, points, seed=points, anchors=True)
     a = _grads(cufk.reconstruct_long, inp, torch.float32, True)
     b = _grads(cufk.reconstruct, inp, torch.float32, True)
-    _check(a, b, 2e-5, 1e-5)
+    # two float32 scans of the same chain with different thread layouts: each is within ~3e-5 nm of
+    # float64 at N = 2051, so they agree to the sum
+    _check(a, b, 6e-5, 1e-5)
 
 
 def test_single_chain_and_empty_batch():

@@ -74,8 +74,11 @@ def test_fused_equals_unfused_sequence():
     loss = ((cufk.reconstruct(L, A, D) - target.to(DEV)) ** 2).sum(-1).mean(-1)
     loss.backward(grad_loss.to(DEV))
     torch.testing.assert_close(got[0], loss.detach().cpu(), rtol=1e-5, atol=0)
+    # the two forwards round differently (the fused kernel keeps the one-CTA scan of the chain, the
+    # block forward its own), and dL/dx = (2/N)(x - t) carries each one's float32 position error
+    # relative to x - t: the gradients agree to the float32 bound of test_fused_loss_matches_float64
     for a, b in zip(got[1:], (L.grad, A.grad, D.grad)):
-        assert rel(a, b.cpu().double()) <= 1e-5
+        assert rel(a, b.cpu().double()) <= 2e-3
 
 
 def test_loss_without_gradients_is_the_same_loss():

@@ -116,9 +116,9 @@ def test_chain_beyond_max_points_is_left_untouched_through_the_c_abi():
     xyz = torch.full((sum(counts), 3), float("nan"), device=DEV)
     lib = _native._LIB
     vp, i64 = ctypes.c_void_p, ctypes.c_int64
-    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
     stream = torch.cuda.current_stream().cuda_stream
-    st = lib.cufkb_block_forward_packed(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, off.data_ptr(), xyz.data_ptr(), 3, 16, stream)
+    st = lib.cufkb_block_forward_packed(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, off.data_ptr(), xyz.data_ptr(), 3, sum(counts), 16, stream)
     torch.cuda.synchronize()
     assert st == 0
     x = xyz.cpu()
@@ -127,3 +127,44 @@ def test_chain_beyond_max_points_is_left_untouched_through_the_c_abi():
     ref = cufk.reconstruct_packed(L, A, D, off).cpu()
     torch.testing.assert_close(x[:12], ref[:12], rtol=0, atol=1e-5)
     torch.testing.assert_close(x[52:], ref[52:], rtol=0, atol=1e-5)
+
+
+def test_offsets_outside_the_packed_arrays_skip_only_those_chains():
+    # Four 10-point chains.  Chain 1's start is made negative (so chain 0 gets a negative count) and
+    # chain 3's end lies far past the packed total: chains 0, 1 and 3 are skipped, chain 2 is
+    # reconstructed, and nothing is written outside the output (guard rows around it stay NaN).
+    counts = [10, 10, 10, 10]
+    total = sum(counts)
+    _, packed, offsets = ragged_inputs(counts, seed=37)
+    L, A, D, G = (packed[k].to(DEV) for k in ("lengths", "angles", "dihedrals", "grad"))
+    bad = offsets.clone()
+    bad[1] = -20
+    bad[4] = 100
+    off = bad.to(DEV)
+    guard = 32
+    base = torch.full((total + 2 * guard, 3), float("nan"), device=DEV)
+    xyz = base[guard : guard + total]
+    lib = _native._LIB
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_packed.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
+    lib.cufkb_block_backward_packed_from_xyz.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
+    stream = torch.cuda.current_stream().cuda_stream
+    st = lib.cufkb_block_forward_packed(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, off.data_ptr(), xyz.data_ptr(), 4, total, 2051, stream)
+    assert st == 0
+    gbase = [torch.full((n + 2 * guard,), float("nan"), device=DEV) for n in (L.numel(), A.numel(), D.numel())]
+    gl, ga, gd = (g[guard:-guard] for g in gbase)
+    st = lib.cufkb_block_backward_packed_from_xyz(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, off.data_ptr(), xyz.data_ptr(),
+                                                  G.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(), 4, total, 2051, stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    b = base.cpu()
+    assert torch.isnan(b[:guard]).all() and torch.isnan(b[guard + total :]).all()
+    x = xyz.cpu()
+    assert torch.isnan(x[:20]).all() and torch.isnan(x[30:]).all()
+    ref = cufk.reconstruct_packed(L, A, D, offsets.to(DEV)).cpu()
+    torch.testing.assert_close(x[20:30], ref[20:30], rtol=0, atol=1e-5)
+    # chain 2's gradients (lengths from 20 - 2, angles from 20 - 4, dihedrals from 20 - 6), the rest NaN
+    for g, start, n in ((gbase[0], 18, 9), (gbase[1], 16, 8), (gbase[2], 14, 7)):
+        h = g.cpu()
+        assert torch.isfinite(h[guard + start : guard + start + n]).all()
+        assert torch.isnan(h[: guard + start]).all() and torch.isnan(h[guard + start + n :]).all()

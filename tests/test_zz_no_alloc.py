@@ -62,3 +62,36 @@ def test_short_chains_and_capacity(lib):
     assert torch.equal(_run(lib, 0, inp, torch.float32, False, static=True), _run(lib, 0, inp, torch.float32, False, static=False))
     # 100 chains of 1e6 points need 100 x 489 segments x 48 B > 2 MiB: rejected before any launch
     assert lib.cufkb_block_forward_long_static(0, 16, 32, 48, None, None, None, 64, 100, 1_000_000, None) == SCRATCH_CAPACITY
+
+
+def test_capacity_boundary_float64(lib):
+    # one segment per chain, 96 B of scratch per chain in float64: 21845 chains fill 2,097,120 of the
+    # 2,097,152 bytes (accepted, twice in a row); one chain more does not fit
+    inp = nerf64.make_inputs(21845, 40, seed=4, dtype=torch.float64)
+    for _ in range(2):
+        got = _run(lib, 1, inp, torch.float64, False, static=True)
+        assert torch.equal(got, _run(lib, 1, inp, torch.float64, False, static=False))
+    assert lib.cufkb_block_forward_long_static(1, 16, 32, 48, None, None, None, 64, 21846, 40, None) == SCRATCH_CAPACITY
+
+
+def test_call_allocates_no_device_memory(lib):
+    # after a warm-up call (module loading is done), a call changes neither torch's allocator
+    # statistics nor the device's free memory
+    inp = nerf64.make_inputs(16, 3000, seed=5)
+    L, A, D = (inp[k].to("cuda") for k in ("lengths", "angles", "dihedrals"))
+    xyz = torch.empty(16, 3000, 3, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        assert lib.cufkb_block_forward_long_static(0, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, xyz.data_ptr(), 16, 3000, s) == 0
+        torch.cuda.synchronize()
+
+    call()
+    stats = torch.cuda.memory_stats()
+    free_before, _ = torch.cuda.mem_get_info()
+    call()
+    free_after, _ = torch.cuda.mem_get_info()
+    after = torch.cuda.memory_stats()
+    assert free_after == free_before
+    for key in ("allocated_bytes.all.current", "reserved_bytes.all.current", "allocation.all.allocated"):
+        assert after.get(key, 0) == stats.get(key, 0), key
