@@ -81,6 +81,7 @@ def parse_args(argv=None):
         help="strong (config 1's split): the batch is split over the ranks; weak: every rank runs the whole batch on its own chains",
     )
     ap.add_argument("--repeats", type=int, default=5, help="timed regions per figure (median reported)")
+    ap.add_argument("--per-graph", type=int, default=10, help="steps captured per CUDA graph (consecutive input sets)")
     ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's own kernels (oracle/_ref)")
     ap.add_argument("--points", type=int, default=POINTS)
     ap.add_argument("--no-e2e", action="store_true")
@@ -315,13 +316,16 @@ def spread(ms_per_step: list[float]) -> dict:
 
 
 class StepGraphs:
-    """Device-resident input sets of one rank and one CUDA graph per set for the step (forward then
-    the backward that reads the forward's xyz, the kernels autograd runs) and for each kernel alone.
-    The sets rotate (total footprint > 3x the 126 MB L2) so that every step reads from HBM."""
+    """Device-resident input sets of one rank and CUDA graphs of `per_graph` consecutive steps (each
+    step the forward then the backward that reads the forward's xyz, the kernels autograd runs), and
+    of each kernel alone.  A graph's steps take consecutive input sets, which rotate (total footprint
+    > 3x the 126 MB L2) so that every step reads from HBM.  Several steps per graph keep the
+    per-replay launch gap of the device (several microseconds) out of the per-step time."""
 
-    def __init__(self, C, host: dict, n: int, dev, stream):
+    def __init__(self, C, host: dict, n: int, dev, stream, per_graph: int = 1):
         b_local = host["lengths"].shape[0]
         self.b_local = b_local
+        self.per_graph = max(1, per_graph)
         self.set_bytes = 4 * b_local * ((n - 1) + (n - 2) + (n - 3) + 3 * n) * 2  # inputs + outputs of a step
         self.n_sets = max(2, min(64, math.ceil(3 * L2_BYTES / max(self.set_bytes, 1))))
         self.sets = []
@@ -331,27 +335,39 @@ class StepGraphs:
             d["dihedrals"] = d["dihedrals"] + 1e-3 * i
             self.sets.append(d)
         torch.cuda.synchronize()
+
+        def fwd(d):
+            return C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
+
+        def bwd(d, xyz):
+            C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, d["grad"])
+
+        def capture(body):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                body()
+            return g
+
         self.step, self.fwd, self.bwd = [], [], []
         with torch.cuda.stream(stream):
             for d in self.sets:  # eager warm-up of both kernels (first-call attribute setup happens here)
-                d["xyz"] = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-                C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
+                d["xyz"] = fwd(d)
+                bwd(d, d["xyz"])
             stream.synchronize()
-            for d in self.sets:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    xyz = C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-                    C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, xyz, d["grad"])
-                self.step.append(g)
-                gf = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gf, stream=stream):
-                    C.block_forward(d["lengths"], d["angles"], d["dihedrals"], None, None, None)
-                self.fwd.append(gf)
-                gb = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gb, stream=stream):
-                    C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["xyz"], d["grad"])
-                self.bwd.append(gb)
+            for i in range(self.n_sets):
+                group = [self.sets[(i + r) % self.n_sets] for r in range(self.per_graph)]
+                self.step.append(capture(lambda group=group: [bwd(d, fwd(d)) for d in group]))
+                self.fwd.append(capture(lambda group=group: [fwd(d) for d in group]))
+                self.bwd.append(capture(lambda group=group: [bwd(d, d["xyz"]) for d in group]))
+            # the unflushed figure: every step of the graph on the first set (its data may stay in L2)
+            first = self.sets[0]
+            self.unflushed = [capture(lambda: [bwd(first, fwd(first)) for _ in range(self.per_graph)])]
         torch.cuda.synchronize()
+
+    def time(self, graphs, steps: int, warmup: int, dist: "Dist", stream, repeats: int) -> list[float]:
+        """ms per step of each repeat (max over ranks), `steps` steps per repeat."""
+        replays = max(1, steps // self.per_graph)
+        return [t / (replays * self.per_graph) for t in time_graphs(graphs, replays, max(1, warmup // self.per_graph), dist, stream, repeats)]
 
 
 def run_ours(args, dist: Dist) -> dict | None:
@@ -366,17 +382,17 @@ def run_ours(args, dist: Dist) -> dict | None:
     stream.wait_stream(torch.cuda.current_stream())
     # synthetic config-1 inputs of this rank: the headline split, and (several ranks) the other one
     host, global_batch = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, args.scaling, dist.world, dist.rank)
-    sg = StepGraphs(C, host, n, dev, stream)
+    per_graph = max(1, min(args.per_graph, args.steps))
+    sg = StepGraphs(C, host, n, dev, stream, per_graph)
     b_local = sg.b_local
 
     sampler = ClockSampler(dev.index)
     with torch.cuda.stream(stream):
         with sampler:
-            step_ms = [t / args.steps for t in time_graphs(sg.step, args.steps, args.warmup, dist, stream, args.repeats)]
-        fwd_ms = [t / args.steps for t in time_graphs(sg.fwd, args.steps, args.warmup, dist, stream, args.repeats)]
-        bwd_ms = [t / args.steps for t in time_graphs(sg.bwd, args.steps, args.warmup, dist, stream, args.repeats)]
-        # the same step on one resident input set (the inputs of a step may still be in L2)
-        unflushed_ms = [t / args.steps for t in time_graphs(sg.step[:1], args.steps, args.warmup, dist, stream, args.repeats)]
+            step_ms = sg.time(sg.step, args.steps, args.warmup, dist, stream, args.repeats)
+        fwd_ms = sg.time(sg.fwd, args.steps, args.warmup, dist, stream, args.repeats)
+        bwd_ms = sg.time(sg.bwd, args.steps, args.warmup, dist, stream, args.repeats)
+        unflushed_ms = sg.time(sg.unflushed, args.steps, args.warmup, dist, stream, args.repeats)
     ms_step = statistics.median(step_ms)
     ms_fwd, ms_bwd = statistics.median(fwd_ms), statistics.median(bwd_ms)
     atoms_total = global_batch * n
@@ -387,9 +403,9 @@ def run_ours(args, dist: Dist) -> dict | None:
     if dist.world > 1:
         other_mode = "weak" if args.scaling == "strong" else "strong"
         host_o, global_o = rank_inputs(lambda b, seed: make_inputs(b, n, seed=seed), args.batch, other_mode, dist.world, dist.rank)
-        sg_o = StepGraphs(C, host_o, n, dev, stream)
+        sg_o = StepGraphs(C, host_o, n, dev, stream, per_graph)
         with torch.cuda.stream(stream):
-            o_ms = [t / args.steps for t in time_graphs(sg_o.step, args.steps, args.warmup, dist, stream, args.repeats)]
+            o_ms = sg_o.time(sg_o.step, args.steps, args.warmup, dist, stream, args.repeats)
         other = {
             "scaling": other_mode,
             "value": global_o * n / (statistics.median(o_ms) * 1e-3),
@@ -485,7 +501,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "value": value,
         "unit": "atoms/s",
         "n_gpus": dist.world,
-        "steps": args.steps,
+        "steps": (args.steps // per_graph) * per_graph,
         "warmup": args.warmup,
         "ms_per_step": ms_step,
         "higher_is_better": True,
@@ -499,14 +515,14 @@ def run_ours(args, dist: Dist) -> dict | None:
             "points": n,
             "per_gpu_batch": b_local,
             "parallelism": f"chains independent, {'each rank its own B' if args.scaling == 'weak' and dist.world > 1 else 'one B split'} x{dist.world}; no collective on the hot path",
-            "l2": f"{sg.n_sets} rotating input/output sets, {sg.n_sets * sg.set_bytes / 2**20:.0f} MiB > L2 (126 MB); unflushed: one set",
-            "timing": f"one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks, median of {args.repeats} repeats of {args.steps} steps",
+            "l2": f"{sg.n_sets} rotating input/output sets, {sg.n_sets * sg.set_bytes / 2**20:.0f} MiB > L2 (126 MB); unflushed: every step on one set",
+            "timing": f"CUDA graphs of {per_graph} steps each (fwd+bwd launches per step, consecutive input sets), CUDA events, max over ranks, median of {args.repeats} repeats of {(args.steps // per_graph) * per_graph} steps",
         },
         "spread": spread(step_ms),
         "unflushed": {"ms_per_step": statistics.median(unflushed_ms), "value": atoms_total / (statistics.median(unflushed_ms) * 1e-3), "spread": spread(unflushed_ms)},
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * (args.steps // per_graph) * per_graph,
         "kernels": "block_forward_kernel + block_backward_xyz_kernel per step (the vector-slot forms)",
         "clocks": sampler.summary(),
     }
@@ -873,18 +889,18 @@ def run_workload(args, dist: Dist) -> dict:
     extra = {}
     with torch.cuda.stream(stream):
         with sampler:
-            ms_total = time_graphs(g_step, args.steps, args.warmup, dist, stream)
+            ms_total = statistics.median(time_graphs(g_step, args.steps, args.warmup, dist, stream, args.repeats))
         if kind == "mse":
             ms_fwd, ms_bwd = ms_total / args.steps, 0.0
-            ms_unfused = time_graphs(g_unfused, args.steps, args.warmup, dist, stream) / args.steps
+            ms_unfused = statistics.median(time_graphs(g_unfused, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
             extra["unfused"] = {
                 "ms_per_step": ms_unfused,
                 "value": batch * points / (ms_unfused * 1e-3),
                 "sequence": "block_forward_kernel, torch loss and dL/dxyz (3 elementwise/reduction kernels), block_backward_xyz_kernel",
             }
         else:
-            ms_fwd = time_graphs(g_fwd, args.steps, args.warmup, dist, stream) / args.steps
-            ms_bwd = time_graphs(g_bwd, args.steps, args.warmup, dist, stream) / args.steps
+            ms_fwd = statistics.median(time_graphs(g_fwd, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
+            ms_bwd = statistics.median(time_graphs(g_bwd, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
     ms_step = ms_total / args.steps
     peak, peak_kind = measured_peak()
     per_kernel = {}
@@ -915,7 +931,7 @@ def run_workload(args, dist: Dist) -> dict:
             "anchors": anchors,
             "per_gpu_batch": b_local,
             "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB",
-            "timing": "one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks",
+            "timing": f"one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks, median of {args.repeats} repeats",
         },
         "roofline": {
             "kernel": dom,

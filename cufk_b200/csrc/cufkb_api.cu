@@ -302,6 +302,9 @@ constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 #define CUFKB_VEC_MAX_GROUPS 7
 #endif
 
+// Longest chain (points) the vector kernels take where a previous-generation kernel exists.
+constexpr int kVecMaxPointsLong = 1024;
+
 struct VecPlan {
   int warps;   // W
   int chains;  // C (chains per CTA)
@@ -518,7 +521,12 @@ int block_backward_xyz_vec(const void* L, const void* A, const void* D, const vo
 template <typename T>
 int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
                        cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
-  if constexpr (sizeof(T) >= 4) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
+  // the vector forward: float32 at every length, float64 up to kVecMaxPointsLong (beyond it the
+  // one-slot-per-step kernel wins: measured on B200 at N = 2051, 71 against 80 us for 2048 chains)
+  if constexpr (sizeof(T) == 4) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
+  if constexpr (sizeof(T) == 8) {
+    if (points <= kVecMaxPointsLong) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
+  }
   const size_t smem = cufkb::block_smem_bytes<T>(points, false);
   auto kernel = cufkb::block_forward_kernel<T>;
   LaunchEnv env;
@@ -553,8 +561,11 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
 template <typename T>
 int block_backward_xyz_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
                             void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
-  // the vector kernel stages xyz and grad rows with one shift: their rows must share the residue mod 16
-  if ((reinterpret_cast<uintptr_t>(xyz) - reinterpret_cast<uintptr_t>(g)) % 16 == 0) {
+  // the vector kernel stages xyz and grad rows with one shift: their rows must share the residue mod
+  // 16.  Up to kVecMaxPointsLong points: beyond, a chain's two staged rows leave room for only ~4
+  // chains per SM and the one-slot-per-step kernel wins (B200, N = 2051 float32: 51 against 55 us
+  // for 2048 chains)
+  if (points <= kVecMaxPointsLong && (reinterpret_cast<uintptr_t>(xyz) - reinterpret_cast<uintptr_t>(g)) % 16 == 0) {
     return block_backward_xyz_vec<T>(L, A, D, p0, fd, nn, xyz, g, gL, gA, gD, batch, points, stream, packed_layout);
   }
   const size_t smem = cufkb::block_smem_bytes<T>(points, true);
