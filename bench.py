@@ -422,12 +422,12 @@ def run_ours(args, dist: Dist) -> dict | None:
     fwd_bpa, bwd_bpa = bytes_per_atom(n)
     atoms_local = b_local * n
     per_kernel = {
-        "block_forward_kernel": (ms_fwd, fwd_bpa),
-        "block_backward_xyz_kernel": (ms_bwd, bwd_bpa),
+        "block_forward_vec_kernel": (ms_fwd, fwd_bpa),
+        "block_backward_xyz_vec_kernel": (ms_bwd, bwd_bpa),
     }
     # bytes the kernels move: the backward reads the forward's xyz (3N) in place of the three input
     # rows (3N - 6) and only three scalars of the inputs
-    moved_bpa = {"block_forward_kernel": fwd_bpa, "block_backward_xyz_kernel": (9 * n - 6) * 4 / n}
+    moved_bpa = {"block_forward_vec_kernel": fwd_bpa, "block_backward_xyz_vec_kernel": (9 * n - 6) * 4 / n}
     dom = max(per_kernel, key=lambda k: per_kernel[k][0])
     ms_dom, bpa_dom = per_kernel[dom]
     achieved = bpa_dom * atoms_local / (ms_dom * 1e-3) / 1e9
@@ -523,7 +523,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "roofline": roofline,
         "e2e": e2e,
         "gpu_launches": 2 * (args.steps // per_graph) * per_graph,
-        "kernels": "block_forward_kernel + block_backward_xyz_kernel per step (the vector-slot forms)",
+        "kernels": "block_forward_vec_kernel + block_backward_xyz_vec_kernel per step",
         "clocks": sampler.summary(),
     }
     if other is not None:
