@@ -48,6 +48,8 @@ METRIC = "fwd+bwd atoms/s (B=4096,N=768 fp32)"
 GLOBAL_BATCH = 4096
 POINTS = 768
 L2_BYTES = 126 * 1024 * 1024
+# chains longer than this take the one-slot-per-step kernels for float64 and for every backward
+VEC_MAX_POINTS_LONG = 1024
 HBM_FALLBACK_GBS = 6650.0
 
 
@@ -823,7 +825,15 @@ def run_workload(args, dist: Dist) -> dict:
     steps_s = points - 3
     if kind == "block":
         fwd_b, bwd_b = (6 * points - 6) * elem, (9 * points - 12) * elem
-        names = ("block_forward_kernel", "block_backward_xyz_kernel" if elem >= 4 else "block_backward_kernel")
+        if elem == 2:
+            # the 16-bit forward also writes float32 positions, which its backward reads
+            names = ("block_forward_kernel", "block_backward_xyz32_kernel")
+        else:
+            vec = elem == 4 or points <= VEC_MAX_POINTS_LONG
+            names = (
+                "block_forward_vec_kernel" if vec else "block_forward_kernel",
+                "block_backward_xyz_vec_kernel" if points <= VEC_MAX_POINTS_LONG else "block_backward_xyz_kernel",
+            )
     elif kind == "mse":
         # one kernel: read lengths/angles/dihedrals and the target, write the three gradient rows
         fwd_b, bwd_b = (9 * points - 12) * elem, 0
@@ -854,11 +864,15 @@ def run_workload(args, dist: Dist) -> dict:
     def fwd(d):
         if kind == "mse":
             return C.block_mse(d["lengths"], d["angles"], d["dihedrals"], None, None, None, d["target"], True)
+        if kind == "block" and elem == 2:
+            return C.block_forward_xyz32(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d))
         if kind == "block":
             return C.block_forward(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d))
         return C.torsion_forward(d["raw"], consts)
 
     def bwd(d, xyz):
+        if kind == "block" and elem == 2:
+            return C.block_backward_from_xyz32(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d), xyz[1], d["grad"])
         if kind == "block":
             return C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d), xyz, d["grad"])
         return C.torsion_backward_from_xyz(d["raw"], consts, xyz, d["grad"])
@@ -874,34 +888,46 @@ def run_workload(args, dist: Dist) -> dict:
             else:
                 bwd(d, d["xyz"])
         stream.synchronize()
-        for d in sets:
+        # `per` consecutive sets per graph, as for the headline: the device's per-replay launch gap
+        # stays out of the per-step time
+        per = max(1, min(args.per_graph, args.steps))
+        for i in range(n_sets):
+            group = [sets[(i + r) % n_sets] for r in range(per)]
             if kind == "mse":
-                bodies = ((g_step, lambda d=d: fwd(d)), (g_unfused, lambda d=d: unfused(d)))
+                bodies = ((g_step, lambda g=group: [fwd(d) for d in g]), (g_unfused, lambda g=group: [unfused(d) for d in g]))
             else:
-                bodies = ((g_step, lambda d=d: bwd(d, fwd(d))), (g_fwd, lambda d=d: fwd(d)), (g_bwd, lambda d=d: bwd(d, d["xyz"])))
+                bodies = (
+                    (g_step, lambda g=group: [bwd(d, fwd(d)) for d in g]),
+                    (g_fwd, lambda g=group: [fwd(d) for d in g]),
+                    (g_bwd, lambda g=group: [bwd(d, d["xyz"]) for d in g]),
+                )
             for lst, body in bodies:
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr, stream=stream):
                     body()
                 lst.append(gr)
     torch.cuda.synchronize()
+    replays = max(1, args.steps // per)
+
+    def ms_per_step(graphs):
+        return statistics.median(time_graphs(graphs, replays, max(1, args.warmup // per), dist, stream, args.repeats)) / (replays * per)
+
     sampler = ClockSampler(dev.index)
     extra = {}
     with torch.cuda.stream(stream):
         with sampler:
-            ms_total = statistics.median(time_graphs(g_step, args.steps, args.warmup, dist, stream, args.repeats))
+            ms_step = ms_per_step(g_step)
         if kind == "mse":
-            ms_fwd, ms_bwd = ms_total / args.steps, 0.0
-            ms_unfused = statistics.median(time_graphs(g_unfused, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
+            ms_fwd, ms_bwd = ms_step, 0.0
+            ms_unfused = ms_per_step(g_unfused)
             extra["unfused"] = {
                 "ms_per_step": ms_unfused,
                 "value": batch * points / (ms_unfused * 1e-3),
                 "sequence": "block_forward_kernel, torch loss and dL/dxyz (3 elementwise/reduction kernels), block_backward_xyz_kernel",
             }
         else:
-            ms_fwd = statistics.median(time_graphs(g_fwd, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
-            ms_bwd = statistics.median(time_graphs(g_bwd, args.steps, args.warmup, dist, stream, args.repeats)) / args.steps
-    ms_step = ms_total / args.steps
+            ms_fwd = ms_per_step(g_fwd)
+            ms_bwd = ms_per_step(g_bwd)
     peak, peak_kind = measured_peak()
     per_kernel = {}
     for name, ms, nbytes in ((names[0], ms_fwd, fwd_b), (names[1], ms_bwd, bwd_b)):
@@ -931,7 +957,7 @@ def run_workload(args, dist: Dist) -> dict:
             "anchors": anchors,
             "per_gpu_batch": b_local,
             "l2": f"{n_sets} rotating input/output sets, {n_sets * set_bytes / 2**20:.0f} MiB",
-            "timing": f"one CUDA graph per input set (fwd+bwd launches), CUDA events, max over ranks, median of {args.repeats} repeats",
+            "timing": f"CUDA graphs of {per} steps each over rotating input sets, CUDA events, max over ranks, median of {args.repeats} repeats",
         },
         "roofline": {
             "kernel": dom,

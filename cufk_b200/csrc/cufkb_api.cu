@@ -22,7 +22,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 88;
+constexpr int kNumKernels = 100;
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -251,7 +251,7 @@ constexpr int dtype_index() {
   return 3;
 }
 
-// Kernel ids for the caches: kind (10) x dtype (4).
+// Kernel ids for the caches: kind x dtype (4).
 enum KernelKind {
   kBlockForward = 0,
   kBlockBackward = 1,
@@ -274,7 +274,12 @@ enum KernelKind {
   kVecBackward1 = 17,
   kVecBackward2 = 18,
   kVecBackward4 = 19,
-  kVecBackward8 = 20
+  kVecBackward8 = 20,
+  // 16-bit backward from float32 positions, per warps per chain
+  kXyz32Backward1 = 21,
+  kXyz32Backward2 = 22,
+  kXyz32Backward4 = 23,
+  kXyz32Backward8 = 24
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
@@ -304,12 +309,6 @@ constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 // Longest chain (points) the vector kernels take where a previous-generation kernel exists.
 constexpr int kVecMaxPointsLong = 1024;
-
-struct VecPlan {
-  int warps;   // W
-  int chains;  // C (chains per CTA)
-  int items;   // K
-};
 
 // The largest shift of a thread range in the batch: known exactly when every chain's output row has
 // the residue mod 16 of the first one ((B, N) rows whose pitch is a multiple of 16 bytes).
@@ -520,9 +519,11 @@ int block_backward_xyz_vec(const void* L, const void* A, const void* D, const vo
 
 template <typename T>
 int block_forward_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
-                       cudaStream_t stream, cufkb::PackedLayout packed_layout = {}) {
+                       cudaStream_t stream, cufkb::PackedLayout packed_layout = {}, float* xyz32 = nullptr) {
   // the vector forward: float32 at every length, float64 up to kVecMaxPointsLong (beyond it the
-  // one-slot-per-step kernel wins: measured on B200 at N = 2051, 71 against 80 us for 2048 chains)
+  // one-slot-per-step kernel wins: measured on B200 at N = 2051, 71 against 80 us for 2048 chains).
+  // The 16-bit types keep the one-slot-per-step kernel: a vector-slot form measured no faster at
+  // config 4 (65.9 against 64.7 us with 2 warps per chain, 84.3 with 4)
   if constexpr (sizeof(T) == 4) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
   if constexpr (sizeof(T) == 8) {
     if (points <= kVecMaxPointsLong) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
@@ -536,9 +537,97 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo);
+  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo, xyz32);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
+}
+
+// ---- 16-bit backward from float32 positions ----
+template <typename T, int W>
+constexpr KernelKind xyz32_kind() {
+  return W == 1 ? kXyz32Backward1 : (W == 2 ? kXyz32Backward2 : (W == 4 ? kXyz32Backward4 : kXyz32Backward8));
+}
+
+template <typename T>
+size_t xyz32_smem(int points, int items) {
+  return cufkb::xyz32_pos_region_bytes<T>(points, items) + cufkb::xyz32_grad_region_bytes<T>(points, items);
+}
+
+template <typename T, int W>
+int launch_xyz32_backward(const cufkb::BlockArgs<T>& args, const float* xyz32, const T* g, T* gL, T* gA, T* gD, int64_t batch, int points, int items,
+                          cudaStream_t stream, cufkb::PackedLayout packed) {
+  auto kernel = cufkb::block_backward_xyz32_kernel<T, W>;
+  const size_t smem = xyz32_smem<T>(points, items);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(xyz32_kind<T, W>(), dtype_index<T>()), batch, points, smem)) return st;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
+  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args, xyz32, g, gL, gA, gD, geo);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+// Warps per chain of the 16-bit float32-position backward: as vec_backward_warps, on its own
+// footprint (float32 positions and the 16-bit grad row).
+template <typename T>
+int xyz32_backward_warps(int64_t batch, int points, int delta) {
+  int w = 1;
+  while (w < cufkb::kMaxWarps && vec_items<float>(points, delta, w) / cufkb::VecSlots<float>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
+  int dev = 0;
+  if (current_device(&dev)) return w;
+  const DeviceCache* d = device_cache(dev);
+  const int sms = d->error ? 148 : d->sm_count;
+  auto resident = [&](int warps) {
+    int err = 0, r = 0;
+    const size_t smem = xyz32_smem<T>(points, vec_items<float>(points, delta, warps));
+    switch (warps) {
+      case 1:
+        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 1>, kXyz32Backward1, dtype_index<T>(), smem, 1, &err);
+        break;
+      case 2:
+        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 2>, kXyz32Backward2, dtype_index<T>(), smem, 2, &err);
+        break;
+      case 4:
+        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 4>, kXyz32Backward4, dtype_index<T>(), smem, 4, &err);
+        break;
+      default:
+        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 8>, kXyz32Backward8, dtype_index<T>(), smem, 8, &err);
+        break;
+    }
+    return err ? 0 : r * warps;
+  };
+  auto busy = [&](int warps) {
+    const int items = vec_items<float>(points, delta, warps);
+    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
+  };
+  while (w < cufkb::kMaxWarps && busy(2 * w)) {
+    const bool low_residency = resident(w) < CUFKB_VEC_BWD_TARGET_WARPS && resident(2 * w) > resident(w);
+    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_BWD_TARGET_WARPS;
+    if (!(low_residency || small_grid)) break;
+    w *= 2;
+  }
+  return w;
+}
+
+template <typename T>
+int block_backward_xyz32_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const float* xyz32,
+                              const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
+  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const int delta = vec_delta_max<float>(xyz32, points, packed.offsets != nullptr);
+  const int w = xyz32_backward_warps<T>(batch, points, delta);
+  const int items = vec_items<float>(points, delta, w);
+  const T* gg = static_cast<const T*>(g);
+  T *l = static_cast<T*>(gL), *a = static_cast<T*>(gA), *d = static_cast<T*>(gD);
+  switch (w) {
+    case 1:
+      return launch_xyz32_backward<T, 1>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
+    case 2:
+      return launch_xyz32_backward<T, 2>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
+    case 4:
+      return launch_xyz32_backward<T, 4>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
+    default:
+      return launch_xyz32_backward<T, 8>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
+  }
 }
 
 template <typename T>
@@ -796,6 +885,11 @@ int check_block_pointers(int dtype, std::initializer_list<const void*> required,
   return CUFKB_SUCCESS;
 }
 
+// The packed total (points of all chains) must be >= 4 B; offsets outside it only skip chains.
+int check_packed_total(int64_t batch, int64_t total_points) {
+  return (total_points < 0 || (batch > 0 && total_points < 4 * batch)) ? CUFKB_ERROR_SHAPE_LIMITS : CUFKB_SUCCESS;
+}
+
 // Packed batches: the offsets array (B+1 int64) must be given, 8-byte aligned.
 int check_offsets(const int64_t* offsets, bool packed) {
   if (!packed) return CUFKB_SUCCESS;
@@ -905,6 +999,71 @@ int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* an
                                           grad_angles, grad_dihedrals, batch, points, stream);
 }
 
+}  // extern "C" (the float32-position dispatchers below are internal)
+
+namespace {
+int block_forward_xyz32_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz,
+                                 float* xyz32, int64_t batch, int64_t points, cufkb_stream_t stream, bool packed, cufkb::PackedLayout layout) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (dtype != CUFKB_FLOAT16 && dtype != CUFKB_BFLOAT16) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {L, A, D, xyz, xyz32}, {L, A, D, p0, fd, nn, xyz})) return st;
+  if (!aligned(xyz32, sizeof(float))) return CUFKB_ERROR_MISALIGNED;
+  if (int st = check_offsets(layout.offsets, packed)) return st;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT16) return block_forward_impl<__half>(L, A, D, p0, fd, nn, xyz, batch, n, s, layout, xyz32);
+  return block_forward_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz, batch, n, s, layout, xyz32);
+}
+
+int block_backward_xyz32_dispatch(int dtype, const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn,
+                                  const float* xyz32, const void* g, void* gL, void* gA, void* gD, int64_t batch, int64_t points, cufkb_stream_t stream,
+                                  bool packed, cufkb::PackedLayout layout) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (dtype != CUFKB_FLOAT16 && dtype != CUFKB_BFLOAT16) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (int st = check_block_pointers(dtype, {L, A, D, xyz32, g, gL, gA, gD}, {L, A, D, p0, fd, nn, g, gL, gA, gD})) return st;
+  if (!aligned(xyz32, sizeof(float))) return CUFKB_ERROR_MISALIGNED;
+  if (int st = check_offsets(layout.offsets, packed)) return st;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT16) return block_backward_xyz32_impl<__half>(L, A, D, p0, fd, nn, xyz32, g, gL, gA, gD, batch, n, s, layout);
+  return block_backward_xyz32_impl<__nv_bfloat16>(L, A, D, p0, fd, nn, xyz32, g, gL, gA, gD, batch, n, s, layout);
+}
+}  // namespace
+
+extern "C" {
+
+int cufkb_block_forward_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
+                              const void* initial_normal, void* xyz, float* xyz32, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  return block_forward_xyz32_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, xyz32, batch, points, stream, false, {});
+}
+
+int cufkb_block_backward_from_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                    const void* first_direction, const void* initial_normal, const float* xyz32, const void* grad_xyz,
+                                    void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
+                                    cufkb_stream_t stream) {
+  return block_backward_xyz32_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz32, grad_xyz, grad_lengths,
+                                       grad_angles, grad_dihedrals, batch, points, stream, false, {});
+}
+
+int cufkb_block_forward_packed_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                     const void* first_direction, const void* initial_normal, const int64_t* chain_points, void* xyz, float* xyz32,
+                                     int64_t batch, int64_t total_points, int64_t max_points, cufkb_stream_t stream) {
+  if (int st = check_packed_total(batch, total_points)) return st;
+  return block_forward_xyz32_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, xyz32, batch, max_points, stream, true,
+                                      cufkb::PackedLayout{chain_points, total_points});
+}
+
+int cufkb_block_backward_packed_from_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                           const void* first_direction, const void* initial_normal, const int64_t* chain_points, const float* xyz32,
+                                           const void* grad_xyz, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
+                                           int64_t total_points, int64_t max_points, cufkb_stream_t stream) {
+  if (int st = check_packed_total(batch, total_points)) return st;
+  return block_backward_xyz32_dispatch(dtype, lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz32, grad_xyz, grad_lengths,
+                                       grad_angles, grad_dihedrals, batch, max_points, stream, true, cufkb::PackedLayout{chain_points, total_points});
+}
+
 int cufkb_block_mse(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
                     const void* initial_normal, const void* target, void* loss, void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch,
                     int64_t points, cufkb_stream_t stream) {
@@ -926,11 +1085,6 @@ int cufkb_block_mse(int dtype, const void* lengths, const void* angles, const vo
   }
   return block_mse_impl<double>(lengths, angles, dihedrals, p0, first_direction, initial_normal, target, loss, grad_lengths, grad_angles, grad_dihedrals,
                                 batch, n, s);
-}
-
-// The packed total (points of all chains) must be >= 4 B; offsets outside it only skip chains.
-int check_packed_total(int64_t batch, int64_t total_points) {
-  return (total_points < 0 || (batch > 0 && total_points < 4 * batch)) ? CUFKB_ERROR_SHAPE_LIMITS : CUFKB_SUCCESS;
 }
 
 int cufkb_block_forward_packed(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0, const void* first_direction,
@@ -1121,7 +1275,7 @@ const char* cufkb_status_string(int status) {
     case CUFKB_ERROR_WORKSPACE:
       return "workspace is smaller than cufkb_block_long_workspace_bytes";
     case CUFKB_ERROR_UNSUPPORTED_DTYPE:
-      return "this path supports float32 and float64 only (chains longer than 2051 points, the fused loss)";
+      return "dtype not served here: chains longer than 2051 points and the fused loss take float32 and float64 only, the float32-position entries float16 and bfloat16 only";
     case CUFKB_ERROR_SCRATCH_CAPACITY:
       return "batch x segments exceeds the 2 MiB static scratch of cufkb_block_forward_long_static";
     default:

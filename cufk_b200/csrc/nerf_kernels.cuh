@@ -503,7 +503,7 @@ __device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* gr
 // --------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
-    block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo) {
+    block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo, float* __restrict__ xyz32) {
   using R = typename ComputeOf<T>::type;
   using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
@@ -516,8 +516,11 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const int N = rows.points, St = N - 3, K = geo.items;
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   T* out = xyz + rows.xyz;
+  // 16-bit types with xyz32: the float slots take that row's residue, so they leave by bulk store too
+  float* out32 = (!kScatter && xyz32 != nullptr) ? xyz32 + rows.xyz : nullptr;
   ChainViews<T> cv;
-  stage_block_inputs<T>(cv, smem, args, rows, kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : 0, tid, nthr);
+  const uintptr_t residue = kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : (reinterpret_cast<uintptr_t>(out32) & 15u);
+  stage_block_inputs<T>(cv, smem, args, rows, residue, tid, nthr);
   // thread 0 builds the first frame while the rows stage; the others read (F, p2) after the scan
   V first_points[9];
   if (tid == 0) {
@@ -553,6 +556,17 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   // ex.frame was written before the barrier that follows the staging
   const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), ex.frame, ex.frame + 9);
   apply_carry<T, V>(cv, W, range);
+  if constexpr (!kScatter) {
+    if (out32 != nullptr) {
+      // the float32 positions as well (the 16-bit xyz backward reads them)
+      fence_proxy_async_smem();
+      __syncthreads();
+      store_row_bulk<float>(out32, reinterpret_cast<const float*>(cv.X), 3 * N, tid, nthr, 0);
+      store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
+      if (tid == 0) bulk_store_wait_read();
+      return;
+    }
+  }
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 

@@ -1,7 +1,11 @@
-// Vector-slot kernels of the block path for 4- and 8-byte types (float32, float64):
+// Vector-slot kernels of the block path:
 //
-//   block_forward_vec_kernel       <- src/cufk/csrc/block.cu:157-204  (xyz from lengths/angles/dihedrals)
+//   block_forward_vec_kernel       <- src/cufk/csrc/block.cu:157-204  (xyz from lengths/angles/dihedrals;
+//                                      float32, float64)
 //   block_backward_xyz_vec_kernel     the gradients of block.cu:206-313 from the forward's xyz
+//                                      (float32, float64)
+//   block_backward_xyz32_kernel       the gradients of block.cu:206-313 for float16/bfloat16 from
+//                                      the float32 positions block_forward_kernel writes beside xyz
 //
 // They compute what block_forward_kernel and block_backward_xyz_kernel compute, with fewer
 // instructions per atom:
@@ -218,18 +222,17 @@ __device__ __forceinline__ void scatter_step_inputs(T* dst, const T* Lr, const T
 
 // The thread's sweep on the library sine/cosine, from global memory (its slots hold positions by
 // now).  Runs only when an angle of the thread lies outside the short reduction's range.
-template <typename T>
-__device__ __noinline__ Affine<T> vec_forward_redo(const BlockArgs<T>& args, const ChainRows& rows, T* X, int a0, int K) {
-  using V = T;
+template <typename T, typename V = typename ComputeOf<T>::type>
+__device__ __noinline__ Affine<V> vec_forward_redo(const BlockArgs<T>& args, const ChainRows& rows, V* X, int a0, int K) {
   Affine<V> P = affine_identity<V>();
   const int N = rows.points;
   for (int k = 0; k < K; ++k) {
     const int a = a0 + k;
     V l = V(0), th = V(0), ph = V(0);
     if (a >= 3 && a < N) {
-      l = args.lengths[rows.lengths + a - 1];
-      th = args.angles[rows.angles + a - 2];
-      ph = args.dihedrals[rows.dihedrals + a - 3];
+      l = to_r<V>(args.lengths[rows.lengths + a - 1]);
+      th = to_r<V>(args.angles[rows.angles + a - 2]);
+      ph = to_r<V>(args.dihedrals[rows.dihedrals + a - 3]);
     }
     V st, ct, sp, cp;
     sincos(th, &st, &ct);
@@ -636,6 +639,241 @@ __global__ void __launch_bounds__(kWarp* W)
   }
   chain_sync<W>();
   write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, u, NT);
+}
+
+// --------------------------------------------------------------------------------------------
+// 16-bit backward from float32 positions
+// --------------------------------------------------------------------------------------------
+// Shared memory of block_backward_xyz32_kernel: the float32 position row (vector slots) in a region
+// that also fits the recompute form's float slots and staged 16-bit input rows, then the 16-bit
+// grad row with room for padding atoms on both sides.
+template <typename T>
+__host__ __device__ inline size_t xyz32_pos_region_bytes(int points, int items) {
+  const size_t vec = vec_row_bytes(points, items, sizeof(float));
+  const size_t redo = block_smem_bytes<T>(points, false);
+  return vec > redo ? vec : redo;
+}
+constexpr int kHalfFrontPad = 48;  // 5 padding atoms of 6 bytes, rounded up
+template <typename T>
+__host__ __device__ inline size_t xyz32_grad_region_bytes(int points, int items) {
+  return kHalfFrontPad + 16 + ((3 * sizeof(T) * static_cast<size_t>(points + items) + 15) & ~size_t(15));
+}
+
+// d lengths/angles/dihedrals rows from gradient slots of the storage type (slot a holds
+// d lengths[a-1], d angles[a-2], d dihedrals[a-3]).
+template <typename T>
+__device__ __forceinline__ void write_grad_slots(const T* X, T* grad_lengths, T* grad_angles, T* grad_dihedrals, const ChainRows& rows, int tid, int nthr) {
+  const int N = rows.points;
+  T* gl = grad_lengths + rows.lengths;
+  T* ga = grad_angles + rows.angles;
+  T* gd = grad_dihedrals + rows.dihedrals;
+#pragma unroll 2
+  for (int i = tid; i < N - 1; i += nthr) {
+    const T* slot = X + 3 * i;
+    gl[i] = slot[3];
+    if (i < N - 2) ga[i] = slot[7];
+    if (i < N - 3) gd[i] = slot[11];
+  }
+}
+
+// The xyz-form backward of float16/bfloat16 chains from the float32 positions the 16-bit forward
+// wrote beside its output (xyz32): a 16-bit position is too coarse for a bond direction, a float32
+// one is what block_backward_xyz_vec_kernel reads in float32.  Positions sit in vector slots as
+// there; the 16-bit grad row is staged as it is (16-byte copies), read element by element and
+// overwritten in place by the three 16-bit gradients of each step.  Degenerate chains take the
+// 16-bit recompute form (block_backward_kernel's code) in the same CTA.
+template <typename T, int W>
+__global__ void __launch_bounds__(kWarp* W)
+    block_backward_xyz32_kernel(BlockArgs<T> args, const float* __restrict__ xyz32, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
+                                T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  static_assert(sizeof(T) == 2, "the float32-position backward serves the 16-bit types");
+  using V = float;
+  constexpr int G = VecSlots<float>::kAtoms;
+  constexpr int NT = kWarp * W;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ VecChainShared<V, W> sh;
+  __shared__ VecBackwardShared<V> bsh;
+  __shared__ CtaExchange<V> ex;  // the recompute form's scans
+
+  const int u = static_cast<int>(threadIdx.x);
+  const int64_t chain = blockIdx.x;
+  const ChainRows rows = chain_rows(geo, chain);
+  if (rows.points == 0) return;  // a packed chain outside [4, geo.points] (uniform over the CTA)
+  const int N = rows.points, K = geo.items;
+  const float* xrow = xyz32 + rows.xyz;
+  const T* grow = grad_xyz + rows.xyz;
+  const uintptr_t residue = reinterpret_cast<uintptr_t>(xrow) & 15u;
+  const int delta = vec_delta<float>(residue);
+  unsigned char* const xregion = smem;
+  unsigned char* const gregion = smem + xyz32_pos_region_bytes<T>(geo.points, K);
+  float* const X = reinterpret_cast<float*>(xregion + kVecFrontPad + residue);
+  const int live = (N + delta + K - 1) / K;
+  const int a0 = u * K - delta;
+  const int pad_end = live * K - delta;
+
+  stage_row_async(xregion + kVecFrontPad, xrow, 3 * N, u, NT);
+  T* const Gh = stage_row_async(gregion + kHalfFrontPad, grow, 3 * N, u, NT);
+  for (int i = u; i < 15; i += NT) Gh[i - 15] = from_r<T>(0.0f);
+  for (int i = 3 * N + u; i < 3 * pad_end; i += NT) Gh[i] = from_r<T>(0.0f);
+  if (u == 0) {
+    const AnchorFrame<V> af = anchor_frame<V>(args.p0, args.first_direction, args.initial_normal);
+    const V l0 = to_r<V>(args.lengths[rows.lengths]);
+    const V l1 = to_r<V>(args.lengths[rows.lengths + 1]);
+    const V a0r = to_r<V>(args.angles[rows.angles]);
+    bsh.first = FirstFrame<V>{af, backward_frame<V>(af, l0, l1, a0r)};
+  }
+  cp_async_wait_all();
+  chain_sync<W>();
+
+  const bool general = bsh.first.bf.general;  // uniform over the CTA
+  bool redo = general;
+  if (!redo) {
+    if (u == 0) {
+      zigzag_padding<V>(X - 3, -3, 5, X, X + 3);
+#pragma unroll
+      for (int i = 0; i < 6; ++i) bsh.g12[i] = to_r<V>(Gh[3 + i]);
+#pragma unroll
+      for (int i = 0; i < 9; ++i) Gh[i] = from_r<T>(0.0f);
+    }
+    if (u == live - 1 && pad_end > N) zigzag_padding<V>(X + 3 * N, 3, pad_end - N, X + 3 * (N - 1), X + 3 * (N - 2));
+    const V o[3] = {X[6], X[7], X[8]};
+    V gsum[3] = {V(0), V(0), V(0)};
+    V msum[3] = {V(0), V(0), V(0)};
+    V xmax2 = V(0);
+    const int groups = K / G;
+    if (u < live) {
+      const float* px = X + 3 * a0;
+      const T* pg = Gh + 3 * a0;
+#pragma unroll 1
+      for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+        SlotGroup<float> xs;
+        load_group(px, xs);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const V xw[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+          const V gg[3] = {to_r<V>(pg[3 * j]), to_r<V>(pg[3 * j + 1]), to_r<V>(pg[3 * j + 2])};
+          xmax2 = fmax(xmax2, dot3(xw, xw));
+          const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
+          V mx[3];
+          cross3(x, gg, mx);
+#pragma unroll
+          for (int i = 0; i < 3; ++i) {
+            gsum[i] = vadd(gsum[i], gg[i]);
+            msum[i] = vadd(msum[i], mx[i]);
+          }
+        }
+      }
+    }
+    V Fs[3], Ms[3];
+    {
+      V mine[6] = {gsum[0], gsum[1], gsum[2], msum[0], msum[1], msum[2]};
+      V after[6];
+      cta_exclusive_suffix<V, 6>(mine, after, sh.warp_sums, W);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        Fs[i] = vadd(after[i], gsum[i]);
+        Ms[i] = vadd(after[3 + i], msum[i]);
+      }
+    }
+    const V F3[3] = {Fs[0], Fs[1], Fs[2]};
+    const V M3[3] = {Ms[0], Ms[1], Ms[2]};
+    V dmin2 = V(1e30), wmin2 = V(1);
+    if (u < live) {
+      V x2[3], up[3], tau[3];
+      {
+        const float* q = X + 3 * (a0 - 2);
+        const V x1[3] = {q[0], q[1], q[2]};
+#pragma unroll
+        for (int i = 0; i < 3; ++i) x2[i] = q[3 + i];
+        const V d[3] = {vsub(x2[0], x1[0]), vsub(x2[1], x1[1]), vsub(x2[2], x1[2])};
+        const V inv = bond_rsqrt(dot3(d, d));
+#pragma unroll
+        for (int i = 0; i < 3; ++i) up[i] = vmul(d[i], inv);
+        const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+        V xf[3];
+        cross3(xr, Fs, xf);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) tau[i] = vsub(Ms[i], xf[i]);
+      }
+      const float* px = X + 3 * a0;
+      T* pg = Gh + 3 * a0;
+#pragma unroll 1
+      for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+        SlotGroup<float> xs;
+        load_group(px, xs);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const V x3[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+          const V gg[3] = {to_r<V>(pg[3 * j]), to_r<V>(pg[3 * j + 1]), to_r<V>(pg[3 * j + 2])};
+          const V d[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+          const V d2 = dot3(d, d);
+          dmin2 = fmin(dmin2, d2);
+          const V inv = bond_rsqrt(d2);
+          const V uc[3] = {vmul(d[0], inv), vmul(d[1], inv), vmul(d[2], inv)};
+          V w[3];
+          cross3(up, uc, w);
+          const V w2 = dot3(w, w);
+          wmin2 = fmin(wmin2, w2);
+          const V d_phi = dot3(up, tau);
+          const V d_len = dot3(uc, Fs);
+          const V d_theta = vneg(vmul(dot3(w, tau), bond_rsqrt(w2)));
+          tau[0] = vfma(d[2], Fs[1], vfma(vneg(d[1]), Fs[2], tau[0]));
+          tau[1] = vfma(d[0], Fs[2], vfma(vneg(d[2]), Fs[0], tau[1]));
+          tau[2] = vfma(d[1], Fs[0], vfma(vneg(d[0]), Fs[1], tau[2]));
+#pragma unroll
+          for (int i = 0; i < 3; ++i) {
+            Fs[i] = vsub(Fs[i], gg[i]);
+            x2[i] = x3[i];
+            up[i] = uc[i];
+          }
+          pg[3 * j] = from_r<T>(d_len);
+          pg[3 * j + 1] = from_r<T>(d_theta);
+          pg[3 * j + 2] = from_r<T>(d_phi);
+        }
+      }
+    }
+    const bool bad = u < live && !(dmin2 >= static_cast<V>(1e-6) * xmax2 && wmin2 >= static_cast<V>(1e-2));
+    redo = chain_any<W>(bad);
+    if (!redo && u == 0) {
+      V out[8];
+      first_frame_grads_world<V>(out, bsh.first.af, bsh.first.bf, bsh.g12, bsh.g12 + 3, F3, M3);
+      Gh[3] = from_r<T>(out[3]);
+      Gh[6] = from_r<T>(out[6]);
+      Gh[7] = from_r<T>(out[7]);
+    }
+  }
+  if (!redo) {
+    chain_sync<W>();
+    write_grad_slots<T>(Gh, grad_lengths, grad_angles, grad_dihedrals, rows, u, NT);
+    return;
+  }
+  // the recompute form of block_backward_kernel: float slots and the staged 16-bit input rows in
+  // the position region, the grad row restaged (the fast form may have written over it)
+  {
+    ChainViews<T> cv;
+    const AnchorFrame<V>& af = bsh.first.af;
+    const BackwardFrame<V>& bf = bsh.first.bf;
+    chain_sync<W>();
+    cv.G = stage_row_async(gregion, grow, 3 * N, u, NT);
+    stage_block_inputs<T>(cv, xregion, args, rows, 0, u, NT);
+    cp_async_wait_all();
+    chain_sync<W>();
+    const int items = (N - 3 + NT - 1) / NT;
+    const StepRange range = step_range(u, items, N - 3);
+    auto step = [&](int s) {
+      V l, th, ph, st, ct, sp, cp;
+      block_step_inputs<T>(cv, s, l, th, ph);
+      step_sincos(th, ph, st, ct, sp, cp);
+      return step_rot(l, st, ct, sp, cp);
+    };
+    if (general) {
+      block_backward_general<T, V>(cv, ex, af, bf, cv.G, range, W, step);
+    } else {
+      block_backward_recompute<true, T, V>(cv, ex, af, bf, cv.G, range, W, step);
+    }
+    chain_sync<W>();
+    write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, u, NT);
+  }
 }
 
 }  // namespace cufkb

@@ -140,15 +140,27 @@ Anchors checked_anchors(const Tensor& p0, const Tensor& fd, const Tensor& nn, co
   return a;
 }
 
-Tensor block_forward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Shape& shape) {
+Tensor block_forward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Shape& shape,
+                          Tensor* xyz32 = nullptr) {
   const c10::cuda::CUDAGuard guard(lengths.device());
   Tensor xyz = torch::empty({shape.batch, shape.points, 3}, lengths.options());
+  if (xyz32 != nullptr) {
+    // float16/bfloat16: the float32 positions as well, for the backward
+    *xyz32 = torch::empty({shape.batch, shape.points, 3}, lengths.options().dtype(torch::kFloat32));
+    check_status(cufkb_block_forward_xyz32(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                           ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
+                                           xyz32->data_ptr<float>(), shape.batch, shape.points, current_stream()),
+                 "reconstruct");
+    return xyz;
+  }
   check_status(cufkb_block_forward(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                    ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
                                    shape.batch, shape.points, current_stream()),
                "reconstruct");
   return xyz;
 }
+
+bool is_16bit(const Tensor& t) { return t.scalar_type() == torch::kHalf || t.scalar_type() == torch::kBFloat16; }
 
 // Backward from the forward's output xyz (float32/float64; 16-bit types recompute).
 std::vector<Tensor> block_backward_xyz_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Tensor& xyz,
@@ -157,6 +169,15 @@ std::vector<Tensor> block_backward_xyz_impl(const Tensor& lengths, const Tensor&
   Tensor gl = torch::empty_like(lengths);
   Tensor ga = torch::empty_like(angles);
   Tensor gd = torch::empty_like(dihedrals);
+  if (is_16bit(lengths) && xyz.scalar_type() == torch::kFloat32) {
+    // float16/bfloat16 with the forward's float32 positions
+    check_status(cufkb_block_backward_from_xyz32(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                                 ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                                 xyz.data_ptr<float>(), grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(),
+                                                 shape.batch, shape.points, current_stream()),
+                 "reconstruct backward");
+    return {gl, ga, gd};
+  }
   check_status(cufkb_block_backward_from_xyz(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                              ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal), xyz.data_ptr(),
                                              grad_points.data_ptr(), gl.data_ptr(), ga.data_ptr(), gd.data_ptr(), shape.batch, shape.points,
@@ -192,8 +213,11 @@ class ReconstructAutograd : public torch::autograd::Function<ReconstructAutograd
     const Anchors a = checked_anchors(opt(p0), opt(first_direction), opt(initial_normal), lengths, shape);
     // the backward reads the output instead of walking the chain again; the version counter of the
     // saved output catches in-place edits of xyz
-    Tensor xyz = block_forward_impl(lengths, angles, dihedrals, a, shape);
-    ctx->save_for_backward({lengths, angles, dihedrals, xyz});
+    // float16/bfloat16 save the float32 positions instead (a 16-bit position is too coarse for the
+    // bond directions the backward takes from it); they are not visible to the caller
+    Tensor xyz32;
+    Tensor xyz = block_forward_impl(lengths, angles, dihedrals, a, shape, is_16bit(lengths) ? &xyz32 : nullptr);
+    ctx->save_for_backward({lengths, angles, dihedrals, xyz32.defined() ? xyz32 : xyz});
     ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
     ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
     ctx->saved_data["initial_normal"] = a.initial_normal.defined() ? c10::IValue(a.initial_normal) : c10::IValue();
@@ -321,9 +345,19 @@ PackedShape check_packed(const Tensor& lengths, const Tensor& angles, const Tens
 }
 
 Tensor packed_forward_impl(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const Anchors& a, const Tensor& chain_points,
-                           const PackedShape& shape) {
+                           const PackedShape& shape, Tensor* xyz32 = nullptr) {
   const c10::cuda::CUDAGuard guard(lengths.device());
   Tensor xyz = torch::empty({shape.total, 3}, lengths.options());
+  if (xyz32 != nullptr) {
+    // float16/bfloat16: the float32 positions as well, for the backward
+    *xyz32 = torch::empty({shape.total, 3}, lengths.options().dtype(torch::kFloat32));
+    check_status(cufkb_block_forward_packed_xyz32(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                                  ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                                  chain_points.data_ptr<int64_t>(), xyz.data_ptr(), xyz32->data_ptr<float>(), shape.batch, shape.total,
+                                                  shape.max_points, current_stream()),
+                 "reconstruct_packed");
+    return xyz;
+  }
   check_status(cufkb_block_forward_packed(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                           ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
                                           chain_points.data_ptr<int64_t>(), xyz.data_ptr(), shape.batch, shape.total, shape.max_points, current_stream()),
@@ -337,6 +371,14 @@ std::vector<Tensor> packed_backward_impl(const Tensor& lengths, const Tensor& an
   Tensor gl = torch::empty_like(lengths);
   Tensor ga = torch::empty_like(angles);
   Tensor gd = torch::empty_like(dihedrals);
+  if (is_16bit(lengths) && xyz.scalar_type() == torch::kFloat32) {
+    check_status(cufkb_block_backward_packed_from_xyz32(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
+                                                        ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
+                                                        chain_points.data_ptr<int64_t>(), xyz.data_ptr<float>(), grad_points.data_ptr(), gl.data_ptr(),
+                                                        ga.data_ptr(), gd.data_ptr(), shape.batch, shape.total, shape.max_points, current_stream()),
+                 "reconstruct_packed backward");
+    return {gl, ga, gd};
+  }
   check_status(cufkb_block_backward_packed_from_xyz(dtype_code(lengths.scalar_type()), lengths.data_ptr(), angles.data_ptr(), dihedrals.data_ptr(),
                                                     ptr_or_null(a.p0), ptr_or_null(a.first_direction), ptr_or_null(a.initial_normal),
                                                     chain_points.data_ptr<int64_t>(), xyz.data_ptr(), grad_points.data_ptr(), gl.data_ptr(),
@@ -352,8 +394,9 @@ class PackedAutograd : public torch::autograd::Function<PackedAutograd> {
     const PackedShape shape = check_packed(lengths, angles, dihedrals, chain_points, max_points);
     const Anchors a{checked_anchor(opt(p0), lengths, "p0"), checked_anchor(opt(first_direction), lengths, "first_direction"),
                     checked_anchor(opt(initial_normal), lengths, "initial_normal")};
-    Tensor xyz = packed_forward_impl(lengths, angles, dihedrals, a, chain_points, shape);
-    ctx->save_for_backward({lengths, angles, dihedrals, chain_points, xyz});
+    Tensor xyz32;  // float16/bfloat16 save the float32 positions instead, as the (B, N) wrapper does
+    Tensor xyz = packed_forward_impl(lengths, angles, dihedrals, a, chain_points, shape, is_16bit(lengths) ? &xyz32 : nullptr);
+    ctx->save_for_backward({lengths, angles, dihedrals, chain_points, xyz32.defined() ? xyz32 : xyz});
     ctx->saved_data["max_points"] = max_points;
     ctx->saved_data["p0"] = a.p0.defined() ? c10::IValue(a.p0) : c10::IValue();
     ctx->saved_data["first_direction"] = a.first_direction.defined() ? c10::IValue(a.first_direction) : c10::IValue();
@@ -488,6 +531,33 @@ std::vector<Tensor> block_backward_from_xyz(const Tensor& lengths, const Tensor&
   return block_backward_xyz_impl(lengths, angles, dihedrals, a, xyz, grad_points, shape);
 }
 
+// float16/bfloat16: the forward with its float32 positions, and the backward that reads them
+// (cufkb_block_forward_xyz32, cufkb_block_backward_from_xyz32)
+std::vector<Tensor> block_forward_xyz32(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                                        const std::optional<Tensor>& fd, const std::optional<Tensor>& nn) {
+  const Shape shape = check_geom(lengths, angles, dihedrals);
+  TORCH_CHECK(is_16bit(lengths), "block_forward_xyz32 supports float16 and bfloat16");
+  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
+  Tensor xyz32;
+  Tensor xyz = block_forward_impl(lengths, angles, dihedrals, a, shape, &xyz32);
+  return {xyz, xyz32};
+}
+
+std::vector<Tensor> block_backward_from_xyz32(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
+                                              const std::optional<Tensor>& fd, const std::optional<Tensor>& nn, const Tensor& xyz32,
+                                              const Tensor& grad_points) {
+  const Shape shape = check_geom(lengths, angles, dihedrals);
+  TORCH_CHECK(is_16bit(lengths), "block_backward_from_xyz32 supports float16 and bfloat16");
+  const Anchors a = checked_anchors(opt(p0), opt(fd), opt(nn), lengths, shape);
+  check_like(grad_points, lengths, "grad_points");
+  check_cuda_float(xyz32, "xyz32");
+  TORCH_CHECK(xyz32.scalar_type() == torch::kFloat32, "xyz32 must be float32");
+  TORCH_CHECK(xyz32.device() == lengths.device(), "xyz32 must be on the same device as reference");
+  TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
+  TORCH_CHECK(xyz32.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "xyz32 must have shape (B, N, 3)");
+  return block_backward_xyz_impl(lengths, angles, dihedrals, a, xyz32, grad_points, shape);
+}
+
 // Fused consumer (cufkb_block_mse): per-chain mean squared distance of the reconstruction to a
 // target and, with_grads, its gradient with respect to lengths, angles and dihedrals.
 std::vector<Tensor> block_mse(const Tensor& lengths, const Tensor& angles, const Tensor& dihedrals, const std::optional<Tensor>& p0,
@@ -552,6 +622,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("block_backward_from_xyz", &block_backward_from_xyz, "backward kernel reading the forward's xyz", pybind11::arg("lengths"),
         pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
         pybind11::arg("xyz"), pybind11::arg("grad_points"));
+  m.def("block_forward_xyz32", &block_forward_xyz32, "16-bit forward kernel writing float32 positions as well", pybind11::arg("lengths"),
+        pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0") = pybind11::none(),
+        pybind11::arg("first_direction") = pybind11::none(), pybind11::arg("initial_normal") = pybind11::none());
+  m.def("block_backward_from_xyz32", &block_backward_from_xyz32, "16-bit backward kernel reading the forward's float32 positions",
+        pybind11::arg("lengths"), pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"),
+        pybind11::arg("initial_normal"), pybind11::arg("xyz32"), pybind11::arg("grad_points"));
   m.def("block_mse", &block_mse, "fused reconstruction + mean squared distance to a target (+ gradients)", pybind11::arg("lengths"),
         pybind11::arg("angles"), pybind11::arg("dihedrals"), pybind11::arg("p0"), pybind11::arg("first_direction"), pybind11::arg("initial_normal"),
         pybind11::arg("target"), pybind11::arg("with_grads"));

@@ -13,14 +13,20 @@ Operators (namespace ``cufk_b200``):
 
 * ``reconstruct(lengths, angles, dihedrals, p0?, first_direction?, initial_normal?) -> xyz``:
   ``(B, N-1)``, ``(B, N-2)``, ``(B, N-3)`` in, ``(B, N, 3)`` out;
+* ``reconstruct_xyz32(lengths, angles, dihedrals, p0?, first_direction?, initial_normal?) ->
+  (xyz, xyz32)``: float16/bfloat16 only; ``xyz`` as ``reconstruct`` gives it and ``xyz32`` the
+  float32 positions before rounding, which its autograd formula hands to the backward (a 16-bit
+  position is too coarse for the bond directions the backward takes from it);
 * ``reconstruct_backward(lengths, angles, dihedrals, p0?, first_direction?, initial_normal?, xyz,
   grad_xyz) -> (grad_lengths, grad_angles, grad_dihedrals)``: reads the forward's output, as the
-  C++ wrapper's backward does (float32/float64; 16-bit types recompute inside the library);
+  C++ wrapper's backward does: ``xyz`` in the inputs' dtype (16-bit types then recompute inside the
+  library) or, for float16/bfloat16, the float32 ``xyz32``;
 * ``torsion_reconstruct(raw_pairs, constants) -> xyz`` and ``torsion_backward(raw_pairs,
   constants, xyz, grad_xyz) -> grad_raw_pairs``, with ``constants`` the nine floats of
   ``torsion.torsion_constants``.
 
-Python helpers with the public signatures: ``reconstruct`` (1-D single-chain inputs included) and
+Python helpers with the public signatures: ``reconstruct`` (1-D single-chain inputs included; the
+16-bit types go through ``reconstruct_xyz32``, the kernels of the C++ wrapper) and
 ``torsion(raw_pairs, bond_lengths, bond_angles)``.  Anchors take no gradient; an anchor that
 requires grad raises the reference's error, as ``cufk_b200.reconstruct`` does.
 """
@@ -87,7 +93,11 @@ def _reconstruct_backward_op(
     xyz: Tensor,
     grad_xyz: Tensor,
 ) -> tuple[Tensor, Tensor, Tensor]:
-    gl, ga, gd = _C.block_backward_from_xyz(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz.contiguous())
+    if xyz.dtype != lengths.dtype:
+        # float16/bfloat16 with the float32 positions of reconstruct_xyz32 (the C++ entry checks both)
+        gl, ga, gd = _C.block_backward_from_xyz32(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz.contiguous())
+    else:
+        gl, ga, gd = _C.block_backward_from_xyz(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz, grad_xyz.contiguous())
     return gl, ga, gd
 
 
@@ -111,6 +121,41 @@ def _reconstruct_grad(ctx, grad_xyz):
 _reconstruct_op.register_autograd(_reconstruct_grad, setup_context=_reconstruct_setup)
 
 
+@torch.library.custom_op("cufk_b200::reconstruct_xyz32", mutates_args=())
+def _reconstruct_xyz32_op(
+    lengths: Tensor,
+    angles: Tensor,
+    dihedrals: Tensor,
+    p0: Optional[Tensor],
+    first_direction: Optional[Tensor],
+    initial_normal: Optional[Tensor],
+) -> tuple[Tensor, Tensor]:
+    xyz, xyz32 = _C.block_forward_xyz32(lengths, angles, dihedrals, p0, first_direction, initial_normal)
+    return xyz, xyz32
+
+
+@_reconstruct_xyz32_op.register_fake
+def _(lengths, angles, dihedrals, p0, first_direction, initial_normal):
+    batch, points = _fake_geometry(lengths, angles, dihedrals)
+    torch._check(lengths.dtype in (torch.float16, torch.bfloat16), lambda: "block_forward_xyz32 supports float16 and bfloat16")
+    return lengths.new_empty((batch, points, 3)), lengths.new_empty((batch, points, 3), dtype=torch.float32)
+
+
+def _reconstruct_xyz32_setup(ctx, inputs, output):
+    lengths, angles, dihedrals, p0, first_direction, initial_normal = inputs
+    ctx.mark_non_differentiable(output[1])
+    ctx.save_for_backward(lengths, angles, dihedrals, p0, first_direction, initial_normal, output[1])
+
+
+def _reconstruct_xyz32_grad(ctx, grad_xyz, _grad_xyz32):
+    lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz32 = ctx.saved_tensors
+    gl, ga, gd = _reconstruct_backward_op(lengths, angles, dihedrals, p0, first_direction, initial_normal, xyz32, grad_xyz)
+    return gl, ga, gd, None, None, None
+
+
+_reconstruct_xyz32_op.register_autograd(_reconstruct_xyz32_grad, setup_context=_reconstruct_xyz32_setup)
+
+
 def reconstruct(
     lengths: Tensor,
     angles: Tensor,
@@ -125,7 +170,11 @@ def reconstruct(
     single = lengths.dim() == 1
     if single:
         lengths, angles, dihedrals = lengths[None], angles[None], dihedrals[None]
-    xyz = _reconstruct_op(lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
+    args = (lengths.contiguous(), angles.contiguous(), dihedrals.contiguous(), p0, first_direction, initial_normal)
+    if lengths.dtype in (torch.float16, torch.bfloat16):
+        xyz = _reconstruct_xyz32_op(*args)[0]
+    else:
+        xyz = _reconstruct_op(*args)
     return xyz[0] if single else xyz
 
 

@@ -67,7 +67,7 @@ enum cufkb_status {
   CUFKB_ERROR_INVALID_VALUE = 8,  /* NULL torsion constants */
   CUFKB_ERROR_CUDA = 9,           /* a CUDA runtime error; see cufkb_last_cuda_error() */
   CUFKB_ERROR_WORKSPACE = 10,     /* workspace smaller than cufkb_block_long_workspace_bytes */
-  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11, /* the long-chain path and the fused loss: float32 and float64 only */
+  CUFKB_ERROR_UNSUPPORTED_DTYPE = 11, /* a dtype the entry point does not serve (long chains, fused loss: float32/float64; *_xyz32: 16-bit) */
   CUFKB_ERROR_SCRATCH_CAPACITY = 12   /* cufkb_block_forward_long_static: call too large for its scratch */
 };
 
@@ -100,12 +100,33 @@ CUFKB_API int cufkb_block_backward(int dtype, const void* lengths, const void* a
  * directions and plane normals of xyz and the running sums of grad_xyz, so the chain is not
  * rebuilt.  Chains whose base frame is not orthonormal, or with a bond angle within ~6 degrees of 0
  * or pi, are recomputed as cufkb_block_backward does.  float16/bfloat16 ignore xyz (a 16-bit
- * position is too coarse for a bond direction) and recompute.  Replaces backward_cuda_impl<T> as
+ * position is too coarse for a bond direction) and recompute; cufkb_block_backward_from_xyz32
+ * takes their float32 positions instead.  Replaces backward_cuda_impl<T> as
  * well; the reference's backward always recomputes the chain. */
 CUFKB_API int cufkb_block_backward_from_xyz(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
                                   const void* first_direction, const void* initial_normal, const void* xyz, const void* grad_xyz,
                                   void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
                                   cufkb_stream_t stream);
+
+/* float16/bfloat16 forward that also writes its float32 positions: xyz (B, N, 3) in the storage
+ * dtype as cufkb_block_forward gives it, and xyz32 (B, N, 3) float32, the positions before rounding.
+ * No counterpart in the reference.  With xyz32, cufkb_block_backward_from_xyz32 computes the
+ * gradients from the positions (bond directions and plane normals) instead of walking the chain
+ * again, as the float32 backward does from its xyz; a 16-bit xyz is too coarse for that.
+ * float16/bfloat16 only (CUFKB_ERROR_UNSUPPORTED_DTYPE otherwise). */
+CUFKB_API int cufkb_block_forward_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                              const void* first_direction, const void* initial_normal, void* xyz, float* xyz32, int64_t batch,
+                              int64_t points, cufkb_stream_t stream);
+
+/* Gradients of sum(grad_xyz * xyz) w.r.t. lengths, angles and dihedrals (float16/bfloat16) from
+ * xyz32 = the float32 positions of cufkb_block_forward_xyz32 with identical arguments; grad_xyz and
+ * the gradients in the storage dtype.  Replaces backward_cuda_impl<T> (src/cufk/csrc/block.cu:331-365)
+ * for the 16-bit types; chains whose base frame is not orthonormal, or with a bond angle within ~6
+ * degrees of 0 or pi, are recomputed as cufkb_block_backward does.  float16/bfloat16 only. */
+CUFKB_API int cufkb_block_backward_from_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                    const void* first_direction, const void* initial_normal, const float* xyz32, const void* grad_xyz,
+                                    void* grad_lengths, void* grad_angles, void* grad_dihedrals, int64_t batch, int64_t points,
+                                    cufkb_stream_t stream);
 
 /* Fused consumer: loss[b] = (1/N) sum_j |xyz_j - target_j|^2 for each chain's reconstruction
  * (as cufkb_block_forward builds it, with the same arguments) and a target (B, N, 3), and, unless
@@ -142,6 +163,19 @@ CUFKB_API int cufkb_block_backward_packed_from_xyz(int dtype, const void* length
                                          const void* xyz, const void* grad_xyz, void* grad_lengths, void* grad_angles,
                                          void* grad_dihedrals, int64_t batch, int64_t total_points, int64_t max_points,
                                          cufkb_stream_t stream);
+
+/* Packed batches of float16/bfloat16 with the float32 positions: cufkb_block_forward_xyz32 and
+ * cufkb_block_backward_from_xyz32 over the packed layout of cufkb_block_forward_packed (xyz and
+ * xyz32 both (total_points, 3)).  No counterpart in the reference. */
+CUFKB_API int cufkb_block_forward_packed_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                     const void* first_direction, const void* initial_normal, const int64_t* chain_points, void* xyz,
+                                     float* xyz32, int64_t batch, int64_t total_points, int64_t max_points, cufkb_stream_t stream);
+
+CUFKB_API int cufkb_block_backward_packed_from_xyz32(int dtype, const void* lengths, const void* angles, const void* dihedrals, const void* p0,
+                                           const void* first_direction, const void* initial_normal, const int64_t* chain_points,
+                                           const float* xyz32, const void* grad_xyz, void* grad_lengths, void* grad_angles,
+                                           void* grad_dihedrals, int64_t batch, int64_t total_points, int64_t max_points,
+                                           cufkb_stream_t stream);
 
 /* xyz (B, N, 3) from raw (sin, cos) pairs; raw row b starts at raw_pairs + b * raw_row_stride
  * elements (any stride >= 0, pairs within a row contiguous). */

@@ -184,3 +184,42 @@ def test_fused_mse_entry_point_validation(lib):
     assert mse(F32, 16, 32, 48, None, None, None, None, 80, None, None, None, 2, 10, None) == NULL_POINTER  # target required
     assert mse(F32, 16, 32, 48, None, None, None, 64, 80, None, None, None, 2, 3, None) == POINT_COUNT
     assert mse(F64, 16, 32, 48, None, None, None, 64, 80, None, None, None, 0, 10, None) == SUCCESS
+
+
+def test_xyz32_entry_points_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_backward_from_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    fwd32 = lib.cufkb_block_forward_xyz32
+    bwd32 = lib.cufkb_block_backward_from_xyz32
+    assert fwd32(F32, 16, 32, 48, None, None, None, 64, 128, 2, 10, None) == 11  # float16/bfloat16 only
+    assert fwd32(F64, 16, 32, 48, None, None, None, 64, 128, 2, 10, None) == 11
+    assert fwd32(F16, 16, 32, 48, None, None, None, 64, None, 2, 10, None) == NULL_POINTER
+    assert fwd32(BF16, 16, 32, 48, None, None, None, 64, 130, 2, 10, None) == MISALIGNED  # float32 positions: 4-byte alignment
+    assert fwd32(F16, 16, 32, 48, None, None, None, 64, 128, 2, 3, None) == POINT_COUNT
+    assert fwd32(F16, 16, 32, 48, None, None, None, 64, 128, 2, 2052, None) == TOO_MANY_STEPS
+    assert fwd32(7, 16, 32, 48, None, None, None, 64, 128, 2, 10, None) == INVALID_DTYPE
+    assert fwd32(BF16, None, None, None, None, None, None, None, None, 0, 10, None) == SUCCESS  # nothing to launch
+    args = [16, 32, 48, None, None, None, 128, 64, 80, 96, 112]
+    assert bwd32(F32, *args, 2, 10, None) == 11
+    assert bwd32(F16, *args[:6], None, *args[7:], 2, 10, None) == NULL_POINTER
+    assert bwd32(F16, *args[:6], 130, *args[7:], 2, 10, None) == MISALIGNED
+    assert bwd32(BF16, *args[:7], 65, *args[8:], 2, 10, None) == MISALIGNED  # grad_xyz: 2-byte alignment
+    assert bwd32(BF16, *args, 2, 2052, None) == TOO_MANY_STEPS
+    assert bwd32(F16, *args, 0, 10, None) == SUCCESS
+    assert b"float16 and bfloat16 only" in lib.cufkb_status_string(11)
+    lib.cufkb_block_forward_packed_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
+    lib.cufkb_block_backward_packed_from_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
+    fwdp = lib.cufkb_block_forward_packed_xyz32
+    bwdp = lib.cufkb_block_backward_packed_from_xyz32
+    assert fwdp(F32, 16, 32, 48, None, None, None, 136, 64, 128, 2, 20, 10, None) == 11
+    assert fwdp(F16, 16, 32, 48, None, None, None, None, 64, 128, 2, 20, 10, None) == NULL_POINTER  # offsets required
+    assert fwdp(F16, 16, 32, 48, None, None, None, 132, 64, 128, 2, 20, 10, None) == MISALIGNED
+    assert fwdp(BF16, 16, 32, 48, None, None, None, 136, 64, 128, 2, 7, 10, None) == SHAPE_LIMITS
+    assert fwdp(BF16, 16, 32, 48, None, None, None, 136, 64, 128, 2, 20, 2052, None) == TOO_MANY_STEPS
+    assert fwdp(BF16, 16, 32, 48, None, None, None, None, 64, 128, 0, 0, 10, None) == SUCCESS
+    assert bwdp(F64, 16, 32, 48, None, None, None, 136, 128, 64, 80, 96, 112, 2, 20, 10, None) == 11
+    assert bwdp(F16, 16, 32, 48, None, None, None, 136, None, 64, 80, 96, 112, 2, 20, 10, None) == NULL_POINTER
+    assert bwdp(F16, 16, 32, 48, None, None, None, 136, 130, 64, 80, 96, 112, 2, 20, 10, None) == MISALIGNED
+    assert bwdp(F16, 16, 32, 48, None, None, None, 136, 128, 64, 80, 96, 112, 2, -1, 10, None) == SHAPE_LIMITS
+    assert bwdp(F16, 16, 32, 48, None, None, None, 136, 128, 64, 80, 96, 112, 0, 0, 10, None) == SUCCESS

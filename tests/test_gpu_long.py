@@ -71,7 +71,7 @@ def test_single_chain_and_empty_batch():
 def test_16bit_is_rejected():
     inp = nerf64.make_inputs(1, 3000, seed=1)
     L, A, D = (inp[k].cuda().half() for k in ("lengths", "angles", "dihedrals"))
-    with pytest.raises(RuntimeError, match="supports float32 and float64 only"):
+    with pytest.raises(RuntimeError, match="take float32 and float64 only"):
         cufk.reconstruct_long(L, A, D)
 
 

@@ -55,6 +55,14 @@ def test_opcheck_reconstruct():
     torch.library.opcheck(torch.ops.cufk_b200.reconstruct.default, (L, A, D, inp["p0"], inp["first_direction"], inp["initial_normal"]))
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_opcheck_reconstruct_xyz32(dtype):
+    inp = inputs(6, 50, dtype, anchors=True, seed=7)
+    L, A, D = (inp[k].clone().requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+    torch.library.opcheck(torch.ops.cufk_b200.reconstruct_xyz32.default, (L, A, D, None, None, None))
+    torch.library.opcheck(torch.ops.cufk_b200.reconstruct_xyz32.default, (L, A, D, inp["p0"], inp["first_direction"], inp["initial_normal"]))
+
+
 def test_opcheck_torsion():
     tin = nerf64.make_torsion_inputs(5, 40, seed=2)
     raw = tin["raw"].to(DEV, torch.float32).requires_grad_(True)

@@ -11,7 +11,7 @@ from torch._subclasses.fake_tensor import FakeTensorMode
 import cufk_b200 as cufk
 from cufk_b200 import ops
 
-OPS = ("reconstruct", "reconstruct_backward", "torsion_reconstruct", "torsion_backward")
+OPS = ("reconstruct", "reconstruct_xyz32", "reconstruct_backward", "torsion_reconstruct", "torsion_backward")
 
 
 def test_operators_registered():
@@ -33,7 +33,15 @@ def test_fake_reconstruct_shapes(dtype):
         assert all(t.dtype == dtype for t in g)
         # the single-chain helper adds and removes the batch dimension
         single = ops.reconstruct(L[0], A[0], D[0])
-        assert single.shape == (100, 3)
+        assert single.shape == (100, 3) and single.dtype == dtype
+        if dtype in (torch.float16, torch.bfloat16):
+            xyz16, xyz32 = torch.ops.cufk_b200.reconstruct_xyz32(L, A, D, None, None, None)
+            assert xyz16.shape == xyz32.shape == (5, 100, 3) and xyz16.dtype == dtype and xyz32.dtype == torch.float32
+            g = torch.ops.cufk_b200.reconstruct_backward(L, A, D, None, None, None, xyz32, torch.empty_like(xyz16))
+            assert [t.shape for t in g] == [L.shape, A.shape, D.shape] and all(t.dtype == dtype for t in g)
+        else:
+            with pytest.raises(Exception, match="supports float16 and bfloat16"):
+                torch.ops.cufk_b200.reconstruct_xyz32(L, A, D, None, None, None)
 
 
 def test_fake_rejects_inconsistent_shapes():
