@@ -10,10 +10,13 @@
 #include "nerf_long.cuh"
 #include "nerf_vec.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <initializer_list>
 #include <mutex>
+#include <type_traits>
+#include <utility>
 
 namespace {
 
@@ -22,7 +25,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 100;
+constexpr int kNumKernels = 92;  // kKindCount x 4 dtypes
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -264,31 +267,19 @@ enum KernelKind {
   kLongSums = 8,
   kLongBackward = 9,
   kBlockMse = 10,
-  // vector-slot kernels, one kind per (warps per chain, chains per CTA) instantiation
-  kVecForward1x1 = 11,
-  kVecForward1x2 = 12,
-  kVecForward1x4 = 13,
-  kVecForward2x1 = 14,
-  kVecForward4x1 = 15,
-  kVecForward8x1 = 16,
-  kVecBackward1 = 17,
-  kVecBackward2 = 18,
-  kVecBackward4 = 19,
-  kVecBackward8 = 20,
-  // 16-bit backward from float32 positions, per warps per chain
-  kXyz32Backward1 = 21,
-  kXyz32Backward2 = 22,
-  kXyz32Backward4 = 23,
-  kXyz32Backward8 = 24
+  // vector-slot kernels: kVecKindBase + family x warp count (vec_kind)
+  kVecKindBase = 11,
+  kKindCount = 23
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
 // ---------------------------------------------------------------------------------------------
-// vector-slot kernels (float32, float64): plan and launch
+// vector-slot kernels: plan and launch
 // ---------------------------------------------------------------------------------------------
-// Warps per chain of the vector kernels; 0 lets the plan choose.  A chain's K atoms per thread are
-// a multiple of G = 16 / sizeof(T) and give an odd number of groups of G (three 16-byte shared
-// accesses per group then fall on distinct banks across each quarter warp).
+// Warps per chain of the vector kernels; 0 lets the plan choose (a count the kernels are built
+// for, kVecWarpCounts).  A chain's K atoms per thread are a multiple of G = 16 / sizeof(slot
+// element) and give an odd number of groups of G (three 16-byte shared accesses per group then fall
+// on distinct banks across each quarter warp).
 #ifndef CUFKB_VEC_FWD_WARPS
 #define CUFKB_VEC_FWD_WARPS 0
 #endif
@@ -328,12 +319,6 @@ int vec_items(int points, int delta, int warps) {
   return groups * G;
 }
 
-template <int W, int C>
-constexpr KernelKind vec_forward_kind() {
-  if constexpr (W == 1) return C == 1 ? kVecForward1x1 : (C == 2 ? kVecForward1x2 : kVecForward1x4);
-  return W == 2 ? kVecForward2x1 : (W == 4 ? kVecForward4x1 : kVecForward8x1);
-}
-
 // Resident CTAs per SM of a kernel instantiation with `smem` bytes of dynamic shared memory.
 template <typename Kernel>
 int resident_ctas(Kernel kernel, int kind, int dtype_idx, size_t smem, int warps_per_cta, int* error) {
@@ -351,170 +336,163 @@ int resident_ctas(Kernel kernel, int kind, int dtype_idx, size_t smem, int warps
   return resident_warps(*d, *k, smem, warps_per_cta) / warps_per_cta;
 }
 
-template <typename T, int W, int C>
-int launch_vec_forward(const cufkb::BlockArgs<T>& args, T* xyz, int64_t batch, int points, int items, cudaStream_t stream, cufkb::PackedLayout packed) {
-  auto kernel = cufkb::block_forward_vec_kernel<T, W, C>;
-  const size_t smem = C * cufkb::vec_row_bytes(points, items, sizeof(T));
-  LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(vec_forward_kind<W, C>(), dtype_index<T>()), batch, points, smem)) return st;
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
-  const unsigned grid = static_cast<unsigned>((batch + C - 1) / C);
-  kernel<<<grid, cufkb::kWarp * W * C, smem, stream>>>(args, xyz, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
-  return CUFKB_SUCCESS;
+// Warp counts per chain the vector kernels are built for.  (Counts 3 and 6, which leave fewer
+// threads without atoms at N = 1026 or 2051, measured slower on B200 than the nearest power of two:
+// per-warp work, staging, scan and stores, outweighs the idle threads.)
+constexpr int kVecWarpCounts[] = {1, 2, 4, 8};
+constexpr int kNumVecWarpCounts = 4;
+constexpr int vec_warp_slot(int w) { return w == 1 ? 0 : (w == 2 ? 1 : (w == 4 ? 2 : 3)); }
+
+// Calls f(std::integral_constant<int, W>()) for the built warp count w.
+template <typename F>
+int with_vec_warps(int w, F&& f) {
+  switch (w) {
+    case 1:
+      return f(std::integral_constant<int, 1>());
+    case 2:
+      return f(std::integral_constant<int, 2>());
+    case 4:
+      return f(std::integral_constant<int, 4>());
+    default:
+      return f(std::integral_constant<int, 8>());
+  }
 }
 
-// Warps per chain of the vector forward: the fewest with at most CUFKB_VEC_MAX_GROUPS groups of G
-// atoms per thread (an odd number of groups), then more while the SM would hold fewer than the
-// target of resident warps (shared memory bounds the chains of one warp), or while the grid offers
-// fewer than the target per SM (small batches), as long as the split leaves every warp busy.
-template <typename T>
-int vec_forward_warps(int64_t batch, int points, int delta) {
+enum VecFamily { kVecForwardFamily = 0, kVecBackwardFamily = 1, kXyz32BackwardFamily = 2 };
+constexpr KernelKind vec_kind(VecFamily f, int w) { return static_cast<KernelKind>(kVecKindBase + f * kNumVecWarpCounts + vec_warp_slot(w)); }
+static_assert(kVecKindBase + 3 * kNumVecWarpCounts == kKindCount, "kind table");
+
+// Warps per chain of a vector kernel whose slots hold `Elem`: the fewest with at most
+// CUFKB_VEC_MAX_GROUPS groups of G atoms per thread, then twice as many while the SM would hold
+// fewer than `target` resident warps and the doubled plan holds more (shared memory bounds the
+// chains of one warp), or while the grid offers fewer than the target per SM (small batches), as
+// long as the doubled plan keeps at least half of its threads on atoms.  resident(w, items) gives
+// the resident warps per SM of the instantiation; `forced` (a build-time override) wins when set.
+template <typename Elem, typename Resident>
+int choose_vec_warps(int64_t batch, int points, int delta, int target, int forced, Resident resident) {
+  constexpr int G = cufkb::VecSlots<Elem>::kAtoms;
+  constexpr int kMax = kVecWarpCounts[kNumVecWarpCounts - 1];
   int w = 1;
-  while (w < cufkb::kMaxWarps && vec_items<T>(points, delta, w) / cufkb::VecSlots<T>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
-  if (CUFKB_VEC_FWD_WARPS > 0) return CUFKB_VEC_FWD_WARPS > w ? CUFKB_VEC_FWD_WARPS : w;
-  int dev = 0;
-  if (current_device(&dev)) return w;
-  const DeviceCache* d = device_cache(dev);
-  const int sms = d->error ? 148 : d->sm_count;
-  auto resident = [&](int warps) {
-    int err = 0, r = 0;
-    const size_t smem = cufkb::vec_row_bytes(points, vec_items<T>(points, delta, warps), sizeof(T));
-    switch (warps) {
-      case 1:
-        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 1, 1>, kVecForward1x1, dtype_index<T>(), smem, 1, &err);
-        break;
-      case 2:
-        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 2, 1>, kVecForward2x1, dtype_index<T>(), smem, 2, &err);
-        break;
-      case 4:
-        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 4, 1>, kVecForward4x1, dtype_index<T>(), smem, 4, &err);
-        break;
-      default:
-        r = resident_ctas(cufkb::block_forward_vec_kernel<T, 8, 1>, kVecForward8x1, dtype_index<T>(), smem, 8, &err);
-        break;
-    }
-    return err ? 0 : r * warps;
-  };
-  // a split is worth it only while the next plan keeps at least half of its threads on atoms
-  auto busy = [&](int warps) {
-    const int items = vec_items<T>(points, delta, warps);
-    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
-  };
-  while (w < cufkb::kMaxWarps && busy(2 * w)) {
-    const bool low_residency = resident(w) < CUFKB_VEC_TARGET_WARPS && resident(2 * w) > resident(w);
-    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_TARGET_WARPS;
+  while (w < kMax && vec_items<Elem>(points, delta, w) / G > CUFKB_VEC_MAX_GROUPS) w *= 2;
+  if (forced > 0) return forced > w ? forced : w;
+  int dev = 0, sms = 148;
+  if (current_device(&dev) == 0) {
+    const DeviceCache* d = device_cache(dev);
+    if (!d->error) sms = d->sm_count;
+  }
+  auto res = [&](int warps) { return resident(warps, vec_items<Elem>(points, delta, warps)); };
+  auto busy = [&](int warps) { return 2 * ceil_div(points + delta, vec_items<Elem>(points, delta, warps)) > int64_t(cufkb::kWarp) * warps; };
+  while (w < kMax && busy(2 * w)) {
+    const bool low_residency = res(w) < target && res(2 * w) > res(w);
+    const bool small_grid = batch * w < int64_t(sms) * target;
     if (!(low_residency || small_grid)) break;
     w *= 2;
   }
   return w;
+}
+
+// Resident warps per SM of family F's kernel with W warps for chains of `points` and `items`.
+template <VecFamily F, typename T>
+int vec_resident(int w, int points, int items);
+
+template <typename T, int W>
+auto vec_kernel(std::integral_constant<VecFamily, kVecForwardFamily>) {
+  return cufkb::block_forward_vec_kernel<T, W, 1>;
+}
+template <typename T, int W>
+auto vec_kernel(std::integral_constant<VecFamily, kVecBackwardFamily>) {
+  return cufkb::block_backward_xyz_vec_kernel<T, W>;
+}
+template <typename T, int W>
+auto vec_kernel(std::integral_constant<VecFamily, kXyz32BackwardFamily>) {
+  return cufkb::block_backward_xyz32_kernel<T, W>;
+}
+
+// Dynamic shared memory of one chain of family F.
+template <VecFamily F, typename T>
+size_t vec_smem(int points, int items) {
+  if constexpr (F == kVecForwardFamily) return cufkb::vec_row_bytes(points, items, sizeof(T));
+  if constexpr (F == kVecBackwardFamily) return 2 * cufkb::vec_row_bytes(points, items, sizeof(T));
+  return cufkb::xyz32_pos_region_bytes<T>(points, items) + cufkb::xyz32_grad_region_bytes<T>(points, items);
+}
+
+template <VecFamily F, typename T>
+int vec_resident(int w, int points, int items) {
+  return with_vec_warps(w, [&](auto wc) {
+    constexpr int W = decltype(wc)::value;
+    int err = 0;
+    const int r = resident_ctas(vec_kernel<T, W>(std::integral_constant<VecFamily, F>()), vec_kind(F, W), dtype_index<T>(), vec_smem<F, T>(points, items), W, &err);
+    return err ? 0 : r * W;
+  });
+}
+
+// Plans family F for a batch: (warps per chain, items per thread).
+template <VecFamily F, typename T>
+std::pair<int, int> vec_plan(int64_t batch, int points, int delta) {
+  using Elem = std::conditional_t<sizeof(T) == 2, float, T>;  // the slot element
+  constexpr bool kForward = F == kVecForwardFamily;
+  const int target = kForward ? CUFKB_VEC_TARGET_WARPS : CUFKB_VEC_BWD_TARGET_WARPS;
+  const int forced = kForward ? CUFKB_VEC_FWD_WARPS : CUFKB_VEC_BWD_WARPS;
+  const int w = choose_vec_warps<Elem>(batch, points, delta, target, forced,
+                                       [&](int ww, int items) { return vec_resident<F, T>(ww, points, items); });
+  return {w, vec_items<Elem>(points, delta, w)};
+}
+
+// Launches family F's kernel with W warps per chain: one CTA per chain.
+template <VecFamily F, typename T, int W, typename... Args>
+int launch_vec(int64_t batch, int points, int items, cudaStream_t stream, Args... args) {
+  auto kernel = vec_kernel<T, W>(std::integral_constant<VecFamily, F>());
+  const size_t smem = vec_smem<F, T>(points, items);
+  LaunchEnv env;
+  if (int st = launch_env(&env, kernel, kernel_id(vec_kind(F, W), dtype_index<T>()), batch, points, smem)) return st;
+  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args...);
+  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  return CUFKB_SUCCESS;
+}
+
+template <typename T>
+cufkb::BlockArgs<T> block_args(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn) {
+  return {static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
+          static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
 }
 
 template <typename T>
 int block_forward_vec(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, void* xyz, int64_t batch, int points,
                       cudaStream_t stream, cufkb::PackedLayout packed) {
-  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
-                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
+  const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
   const int delta = vec_delta_max<T>(xyz, points, packed.offsets != nullptr);
-  const int w = vec_forward_warps<T>(batch, points, delta);
-  const int items = vec_items<T>(points, delta, w);
-  T* out = static_cast<T*>(xyz);
-  switch (w) {
-    case 1:
-      return launch_vec_forward<T, 1, 1>(args, out, batch, points, items, stream, packed);
-    case 2:
-      return launch_vec_forward<T, 2, 1>(args, out, batch, points, items, stream, packed);
-    case 4:
-      return launch_vec_forward<T, 4, 1>(args, out, batch, points, items, stream, packed);
-    default:
-      return launch_vec_forward<T, 8, 1>(args, out, batch, points, items, stream, packed);
-  }
-}
-
-// Resident warps per SM of a kernel instantiation with `smem` bytes of dynamic shared memory.
-template <typename Kernel>
-int vec_resident_warps(Kernel kernel, int kind, int dtype_idx, size_t smem, int warps_per_cta, int* error) {
-  return resident_ctas(kernel, kind, dtype_idx, smem, warps_per_cta, error) * warps_per_cta;
-}
-
-template <typename T, int W>
-int launch_vec_backward(const cufkb::BlockArgs<T>& args, const T* xyz, const T* g, T* gL, T* gA, T* gD, int64_t batch, int points, int items,
-                        cudaStream_t stream, cufkb::PackedLayout packed_layout) {
-  auto kernel = cufkb::block_backward_xyz_vec_kernel<T, W>;
-  const size_t smem = 2 * cufkb::vec_row_bytes(points, items, sizeof(T));
-  constexpr KernelKind kind = W == 1 ? kVecBackward1 : (W == 2 ? kVecBackward2 : (W == 4 ? kVecBackward4 : kVecBackward8));
-  LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(kind, dtype_index<T>()), batch, points, smem)) return st;
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed_layout};
-  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args, xyz, g, gL, gA, gD, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
-  return CUFKB_SUCCESS;
-}
-
-// Warps per chain of the vector xyz backward: as vec_forward_warps, on its own footprint.
-template <typename T>
-int vec_backward_warps(int64_t batch, int points, int delta) {
-  if (CUFKB_VEC_BWD_WARPS > 0) return CUFKB_VEC_BWD_WARPS;
-  int dev = 0;
-  if (current_device(&dev)) return 2;
-  const DeviceCache* d = device_cache(dev);
-  const int sms = d->error ? 148 : d->sm_count;
-  int w = 1;
-  while (w < cufkb::kMaxWarps && vec_items<T>(points, delta, w) / cufkb::VecSlots<T>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
-  auto resident = [&](int warps) {
-    int err = 0;
-    const size_t smem = 2 * cufkb::vec_row_bytes(points, vec_items<T>(points, delta, warps), sizeof(T));
-    int r = 0;
-    switch (warps) {
-      case 1:
-        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 1>, kVecBackward1, dtype_index<T>(), smem, 1, &err);
-        break;
-      case 2:
-        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 2>, kVecBackward2, dtype_index<T>(), smem, 2, &err);
-        break;
-      case 4:
-        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 4>, kVecBackward4, dtype_index<T>(), smem, 4, &err);
-        break;
-      default:
-        r = vec_resident_warps(cufkb::block_backward_xyz_vec_kernel<T, 8>, kVecBackward8, dtype_index<T>(), smem, 8, &err);
-        break;
-    }
-    return err ? 0 : r;
-  };
-  auto busy = [&](int warps) {
-    const int items = vec_items<T>(points, delta, warps);
-    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
-  };
-  while (w < cufkb::kMaxWarps && busy(2 * w)) {
-    const bool low_residency = resident(w) < CUFKB_VEC_BWD_TARGET_WARPS && resident(2 * w) > resident(w);
-    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_BWD_TARGET_WARPS;
-    if (!(low_residency || small_grid)) break;
-    w *= 2;
-  }
-  return w;
+  const auto [w, items] = vec_plan<kVecForwardFamily, T>(batch, points, delta);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
+  return with_vec_warps(w, [&](auto wc) {
+    return launch_vec<kVecForwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
+  });
 }
 
 template <typename T>
 int block_backward_xyz_vec(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const void* xyz, const void* g,
-                           void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed_layout) {
-  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
-                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const int delta = vec_delta_max<T>(xyz, points, packed_layout.offsets != nullptr);
-  const int w = vec_backward_warps<T>(batch, points, delta);
-  const int items = vec_items<T>(points, delta, w);
-  const T* x = static_cast<const T*>(xyz);
-  const T* gg = static_cast<const T*>(g);
-  T *l = static_cast<T*>(gL), *a = static_cast<T*>(gA), *d = static_cast<T*>(gD);
-  switch (w) {
-    case 1:
-      return launch_vec_backward<T, 1>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
-    case 2:
-      return launch_vec_backward<T, 2>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
-    case 4:
-      return launch_vec_backward<T, 4>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
-    default:
-      return launch_vec_backward<T, 8>(args, x, gg, l, a, d, batch, points, items, stream, packed_layout);
-  }
+                           void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
+  const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
+  const int delta = vec_delta_max<T>(xyz, points, packed.offsets != nullptr);
+  const auto [w, items] = vec_plan<kVecBackwardFamily, T>(batch, points, delta);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
+  return with_vec_warps(w, [&](auto wc) {
+    return launch_vec<kVecBackwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, static_cast<const T*>(xyz), static_cast<const T*>(g),
+                                                                   static_cast<T*>(gL), static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  });
+}
+
+// The 16-bit backward from the forward's float32 positions.
+template <typename T>
+int block_backward_xyz32_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const float* xyz32,
+                              const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
+  const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
+  const int delta = vec_delta_max<float>(xyz32, points, packed.offsets != nullptr);
+  const auto [w, items] = vec_plan<kXyz32BackwardFamily, T>(batch, points, delta);
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
+  return with_vec_warps(w, [&](auto wc) {
+    return launch_vec<kXyz32BackwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, xyz32, static_cast<const T*>(g),
+                                                                     static_cast<T*>(gL), static_cast<T*>(gA), static_cast<T*>(gD), geo);
+  });
 }
 
 template <typename T>
@@ -522,8 +500,9 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
                        cudaStream_t stream, cufkb::PackedLayout packed_layout = {}, float* xyz32 = nullptr) {
   // the vector forward: float32 at every length, float64 up to kVecMaxPointsLong (beyond it the
   // one-slot-per-step kernel wins: measured on B200 at N = 2051, 71 against 80 us for 2048 chains).
-  // The 16-bit types keep the one-slot-per-step kernel: a vector-slot form measured no faster at
-  // config 4 (65.9 against 64.7 us with 2 warps per chain, 84.3 with 4)
+  // The 16-bit types keep the one-slot-per-step kernel, which writes the float32 positions as
+  // well when asked: a vector-slot form measured no faster at config 4 (65.9 / 67.0 / 84.3 us with
+  // 2 / 3 / 4 warps per chain against 64.7)
   if constexpr (sizeof(T) == 4) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
   if constexpr (sizeof(T) == 8) {
     if (points <= kVecMaxPointsLong) return block_forward_vec<T>(L, A, D, p0, fd, nn, xyz, batch, points, stream, packed_layout);
@@ -540,94 +519,6 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo, xyz32);
   if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
   return CUFKB_SUCCESS;
-}
-
-// ---- 16-bit backward from float32 positions ----
-template <typename T, int W>
-constexpr KernelKind xyz32_kind() {
-  return W == 1 ? kXyz32Backward1 : (W == 2 ? kXyz32Backward2 : (W == 4 ? kXyz32Backward4 : kXyz32Backward8));
-}
-
-template <typename T>
-size_t xyz32_smem(int points, int items) {
-  return cufkb::xyz32_pos_region_bytes<T>(points, items) + cufkb::xyz32_grad_region_bytes<T>(points, items);
-}
-
-template <typename T, int W>
-int launch_xyz32_backward(const cufkb::BlockArgs<T>& args, const float* xyz32, const T* g, T* gL, T* gA, T* gD, int64_t batch, int points, int items,
-                          cudaStream_t stream, cufkb::PackedLayout packed) {
-  auto kernel = cufkb::block_backward_xyz32_kernel<T, W>;
-  const size_t smem = xyz32_smem<T>(points, items);
-  LaunchEnv env;
-  if (int st = launch_env(&env, kernel, kernel_id(xyz32_kind<T, W>(), dtype_index<T>()), batch, points, smem)) return st;
-  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
-  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args, xyz32, g, gL, gA, gD, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
-  return CUFKB_SUCCESS;
-}
-
-// Warps per chain of the 16-bit float32-position backward: as vec_backward_warps, on its own
-// footprint (float32 positions and the 16-bit grad row).
-template <typename T>
-int xyz32_backward_warps(int64_t batch, int points, int delta) {
-  int w = 1;
-  while (w < cufkb::kMaxWarps && vec_items<float>(points, delta, w) / cufkb::VecSlots<float>::kAtoms > CUFKB_VEC_MAX_GROUPS) w *= 2;
-  int dev = 0;
-  if (current_device(&dev)) return w;
-  const DeviceCache* d = device_cache(dev);
-  const int sms = d->error ? 148 : d->sm_count;
-  auto resident = [&](int warps) {
-    int err = 0, r = 0;
-    const size_t smem = xyz32_smem<T>(points, vec_items<float>(points, delta, warps));
-    switch (warps) {
-      case 1:
-        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 1>, kXyz32Backward1, dtype_index<T>(), smem, 1, &err);
-        break;
-      case 2:
-        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 2>, kXyz32Backward2, dtype_index<T>(), smem, 2, &err);
-        break;
-      case 4:
-        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 4>, kXyz32Backward4, dtype_index<T>(), smem, 4, &err);
-        break;
-      default:
-        r = resident_ctas(cufkb::block_backward_xyz32_kernel<T, 8>, kXyz32Backward8, dtype_index<T>(), smem, 8, &err);
-        break;
-    }
-    return err ? 0 : r * warps;
-  };
-  auto busy = [&](int warps) {
-    const int items = vec_items<float>(points, delta, warps);
-    return 2 * ceil_div(points + delta, items) > cufkb::kWarp * warps;
-  };
-  while (w < cufkb::kMaxWarps && busy(2 * w)) {
-    const bool low_residency = resident(w) < CUFKB_VEC_BWD_TARGET_WARPS && resident(2 * w) > resident(w);
-    const bool small_grid = batch * w < int64_t(sms) * CUFKB_VEC_BWD_TARGET_WARPS;
-    if (!(low_residency || small_grid)) break;
-    w *= 2;
-  }
-  return w;
-}
-
-template <typename T>
-int block_backward_xyz32_impl(const void* L, const void* A, const void* D, const void* p0, const void* fd, const void* nn, const float* xyz32,
-                              const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
-  cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
-                           static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
-  const int delta = vec_delta_max<float>(xyz32, points, packed.offsets != nullptr);
-  const int w = xyz32_backward_warps<T>(batch, points, delta);
-  const int items = vec_items<float>(points, delta, w);
-  const T* gg = static_cast<const T*>(g);
-  T *l = static_cast<T*>(gL), *a = static_cast<T*>(gA), *d = static_cast<T*>(gD);
-  switch (w) {
-    case 1:
-      return launch_xyz32_backward<T, 1>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
-    case 2:
-      return launch_xyz32_backward<T, 2>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
-    case 4:
-      return launch_xyz32_backward<T, 4>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
-    default:
-      return launch_xyz32_backward<T, 8>(args, xyz32, gg, l, a, d, batch, points, items, stream, packed);
-  }
 }
 
 template <typename T>

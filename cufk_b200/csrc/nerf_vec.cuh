@@ -645,12 +645,13 @@ __global__ void __launch_bounds__(kWarp* W)
 // 16-bit backward from float32 positions
 // --------------------------------------------------------------------------------------------
 // Shared memory of block_backward_xyz32_kernel: the float32 position row (vector slots) in a region
-// that also fits the recompute form's float slots and staged 16-bit input rows, then the 16-bit
-// grad row with room for padding atoms on both sides.
+// that also fits the recompute form's float slots, then the 16-bit grad row with room for padding
+// atoms on both sides.
 template <typename T>
 __host__ __device__ inline size_t xyz32_pos_region_bytes(int points, int items) {
+  // the recompute form's float slots fit in the vector row (its input rows stay in global memory)
   const size_t vec = vec_row_bytes(points, items, sizeof(float));
-  const size_t redo = block_smem_bytes<T>(points, false);
+  const size_t redo = slot_bytes(points, sizeof(float));
   return vec > redo ? vec : redo;
 }
 constexpr int kHalfFrontPad = 48;  // 5 padding atoms of 6 bytes, rounded up
@@ -847,15 +848,19 @@ __global__ void __launch_bounds__(kWarp* W)
     write_grad_slots<T>(Gh, grad_lengths, grad_angles, grad_dihedrals, rows, u, NT);
     return;
   }
-  // the recompute form of block_backward_kernel: float slots and the staged 16-bit input rows in
-  // the position region, the grad row restaged (the fast form may have written over it)
+  // the recompute form of block_backward_kernel: float slots in the position region, the 16-bit
+  // input rows read from global memory (a rare path; staging them would cost every chain shared
+  // memory), the grad row restaged (the fast form may have written over it)
   {
     ChainViews<T> cv;
     const AnchorFrame<V>& af = bsh.first.af;
     const BackwardFrame<V>& bf = bsh.first.bf;
     chain_sync<W>();
     cv.G = stage_row_async(gregion, grow, 3 * N, u, NT);
-    stage_block_inputs<T>(cv, xregion, args, rows, 0, u, NT);
+    cv.X = reinterpret_cast<float*>(xregion);
+    cv.row[0] = args.lengths + rows.lengths;
+    cv.row[1] = args.angles + rows.angles;
+    cv.row[2] = args.dihedrals + rows.dihedrals;
     cp_async_wait_all();
     chain_sync<W>();
     const int items = (N - 3 + NT - 1) / NT;
