@@ -239,6 +239,53 @@ __device__ __forceinline__ Affine<V> sweep_local_prefix(const ChainViews<T>& cv,
   return P;
 }
 
+// Two floats rounded to a 16-bit type, packed low element first.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+  uint32_t u;
+  if constexpr (std::is_same_v<T, __half>) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    memcpy(&u, &h, sizeof u);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    memcpy(&u, &h, sizeof u);
+  }
+  return u;
+}
+
+// Residue mod 16 of the float slots of a 16-bit forward: the float32 output row's when there is
+// one, else twice the 16-bit row's, so that the slots line up with the 16-bit row for
+// store_half_row (and with a float32 row of the same shape, whose residue is that too).
+__device__ __forceinline__ uintptr_t half_slot_residue(const void* out16, const float* out32) {
+  return out32 != nullptr ? (reinterpret_cast<uintptr_t>(out32) & 15u) : ((2u * (reinterpret_cast<uintptr_t>(out16) & 15u)) & 15u);
+}
+
+// A 16-bit row from `count` floats in shared memory: where X + e and out + e line up (X at a
+// 16-byte boundary where out is at an 8-byte one), four elements per thread and iteration (one
+// 16-byte shared load, two packed roundings, one 8-byte global store; consecutive threads write
+// consecutive 8 bytes); element by element at the ragged ends, and throughout when they do not.
+template <typename T>
+__device__ __forceinline__ void store_half_row(T* out, const float* X, int count, int tid, int nthr) {
+  const uintptr_t o = reinterpret_cast<uintptr_t>(out);
+  const int head = min(static_cast<int>(((8u - (o & 7u)) & 7u) / 2u), count);
+  if ((reinterpret_cast<uintptr_t>(X + head) & 15u) != 0) {
+#pragma unroll 4
+    for (int e = tid; e < count; e += nthr) out[e] = from_r<T>(X[e]);
+    return;
+  }
+  const int chunks = (count - head) / 4;
+  const float4* src = reinterpret_cast<const float4*>(X + head);
+  uint2* dst = reinterpret_cast<uint2*>(out + head);
+#pragma unroll 4
+  for (int c = tid; c < chunks; c += nthr) {
+    const float4 v = src[c];
+    dst[c] = make_uint2(pack_pair<T>(v.x, v.y), pack_pair<T>(v.z, v.w));
+  }
+  if (tid < head) out[tid] = from_r<T>(X[tid]);
+  const int tail = head + 4 * chunks;
+  if (tid < count - tail) out[tail + tid] = from_r<T>(X[tail + tid]);
+}
+
 // Writes the slot array (3N values in R) to the output row.  Scatter types hold final T values
 // with the row's residue mod 16, so the row leaves in one bulk store; 16-bit types convert.
 template <typename T, typename R>
@@ -250,8 +297,7 @@ __device__ __forceinline__ void store_xyz_row(T* out, const R* X, int N, int tid
     if (tid == 0) bulk_store_wait_read();
   } else {
     __syncthreads();
-#pragma unroll 4
-    for (int e = tid; e < 3 * N; e += nthr) out[e] = from_r<T>(X[e]);
+    store_half_row<T>(out, X, 3 * N, tid, nthr);
   }
 }
 
@@ -516,10 +562,11 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const int N = rows.points, St = N - 3, K = geo.items;
   const int tid = threadIdx.x, nthr = blockDim.x, nwarps = nthr / kWarp;
   T* out = xyz + rows.xyz;
-  // 16-bit types with xyz32: the float slots take that row's residue, so they leave by bulk store too
+  // 16-bit types: the float slots take half_slot_residue's residue (with xyz32, that row's, so that
+  // they leave by bulk store too)
   float* out32 = (!kScatter && xyz32 != nullptr) ? xyz32 + rows.xyz : nullptr;
   ChainViews<T> cv;
-  const uintptr_t residue = kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : (reinterpret_cast<uintptr_t>(out32) & 15u);
+  const uintptr_t residue = kScatter ? (reinterpret_cast<uintptr_t>(out) & 15u) : half_slot_residue(out, out32);
   stage_block_inputs<T>(cv, smem, args, rows, residue, tid, nthr);
   // thread 0 builds the first frame while the rows stage; the others read (F, p2) after the scan
   V first_points[9];
@@ -1025,7 +1072,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     cv.X = reinterpret_cast<R*>(smem + (reinterpret_cast<uintptr_t>(out) & 15u));
     scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
   } else {
-    cv.X = reinterpret_cast<R*>(smem);
+    cv.X = reinterpret_cast<R*>(smem + half_slot_residue(out, nullptr));  // lines up with out for store_half_row
     cv.row[0] = stage_row_async(smem + slot_bytes(N, sizeof(R)), raw, 2 * St, tid, nthr);
   }
   V F[9], p1[3], p2[3];

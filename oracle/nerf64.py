@@ -1,4 +1,8 @@
-"""Float64 CPU restatement of cufk's reconstruction path: the parity oracle.
+"""Float64 restatement of cufk's reconstruction path: the parity oracle.
+
+It computes on the device of its inputs: on the CPU, and, in GPU tests at full configuration
+sizes, in float64 on the GPU (the same arithmetic; the sequential loop over a chain's steps is
+what makes the CPU slow there).
 
 TEST INFRASTRUCTURE ONLY.  Nothing in the product package (``cufk_b200``) imports, calls or
 executes this module; only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
@@ -96,11 +100,11 @@ def local_transform64(length, s, c, S, C):
     return rows, t
 
 
-def _anchors(p0, first_direction, initial_normal):
+def _anchors(p0, first_direction, initial_normal, device="cpu"):
     def one(x, default):
         if x is None:
-            return torch.tensor(default, dtype=F64)
-        return x.detach().to("cpu", F64)
+            return torch.tensor(default, dtype=F64, device=device)
+        return x.detach().to(device, F64)
 
     return (
         one(p0, DEFAULT_P0),
@@ -118,8 +122,8 @@ def nerf64_sincos(lengths, sin_t, cos_t, sin_p, cos_p, l0, l1, a0, p0, first_dir
     """
     ff = first_frame64(l0, l1, a0, p0, first_direction, initial_normal)
     b, steps = lengths.shape
-    m = torch.eye(3, dtype=F64).expand(b, 3, 3)
-    v = torch.zeros(b, 3, dtype=F64)
+    m = torch.eye(3, dtype=F64, device=lengths.device).expand(b, 3, 3)
+    v = torch.zeros(b, 3, dtype=F64, device=lengths.device)
     pts = []
     frame, p2 = ff["frame"], ff["p2"]
     for k in range(steps):
@@ -133,7 +137,7 @@ def nerf64_sincos(lengths, sin_t, cos_t, sin_p, cos_p, l0, l1, a0, p0, first_dir
 
 
 def reconstruct64(lengths, angles, dihedrals, p0=None, first_direction=None, initial_normal=None):
-    """cufk.reconstruct (reconstruct.py:29-81) restated in float64 on the CPU.
+    """cufk.reconstruct (reconstruct.py:29-81) restated in float64, on the inputs' device.
 
     Accepts (N-1,)/(N-2,)/(N-3,) or (B, ...) inputs of any float dtype; computes in float64 and
     returns (N, 3) or (B, N, 3) float64.  Differentiable w.r.t. lengths/angles/dihedrals.
@@ -146,7 +150,7 @@ def reconstruct64(lengths, angles, dihedrals, p0=None, first_direction=None, ini
     D = dihedrals.to(F64)
     if L.shape[1] < 3:
         raise ValueError("point_count must be >= 4")
-    p0_, fd_, nn_ = _anchors(p0, first_direction, initial_normal)
+    p0_, fd_, nn_ = _anchors(p0, first_direction, initial_normal, L.device)
     xyz = nerf64_sincos(
         L[:, 2:],
         torch.sin(A[:, 1:]),
@@ -179,12 +183,12 @@ def reconstruct64_anchor_grads(lengths, angles, dihedrals, grad_xyz, p0, first_d
     The reference itself rejects anchor gradients (extension_utils.cuh:81); this is the check for
     the extension that provides them.  Returns (xyz, d p0, d first_direction, d initial_normal)."""
     L, A, D = (x.detach().to(F64) for x in (lengths, angles, dihedrals))
-    anchors = [x.detach().to("cpu", F64).requires_grad_(True) for x in (p0, first_direction, initial_normal)]
+    anchors = [x.detach().to(L.device, F64).requires_grad_(True) for x in (p0, first_direction, initial_normal)]
     xyz = nerf64_sincos(L[:, 2:], torch.sin(A[:, 1:]), torch.cos(A[:, 1:]), torch.sin(D), torch.cos(D), L[:, 0], L[:, 1], A[:, 0], *anchors)
     grads = torch.autograd.grad((xyz * grad_xyz.detach().to(F64)).sum(), anchors, allow_unused=True)
     # an anchor the frame does not use (the initial normal when it is parallel to the first
     # direction) has a zero gradient
-    return (xyz.detach(), *(torch.zeros(3, dtype=F64) if gr is None else gr for gr in grads))
+    return (xyz.detach(), *(torch.zeros(3, dtype=F64, device=L.device) if gr is None else gr for gr in grads))
 
 
 def block_backward64(lengths, angles, dihedrals, grad_xyz, p0=None, first_direction=None, initial_normal=None):
@@ -199,7 +203,8 @@ def block_backward64(lengths, angles, dihedrals, grad_xyz, p0=None, first_direct
     A = angles.to(F64)
     D = dihedrals.to(F64)
     g = grad_xyz.to(F64)
-    p0_, fd_, nn_ = _anchors(p0, first_direction, initial_normal)
+    dev = g.device
+    p0_, fd_, nn_ = _anchors(p0, first_direction, initial_normal, dev)
     b, npts = g.shape[0], g.shape[1]
     steps = npts - 3
     ff = first_frame64(L[:, 0], L[:, 1], A[:, 0], p0_, fd_, nn_)
@@ -208,8 +213,8 @@ def block_backward64(lengths, angles, dihedrals, grad_xyz, p0=None, first_direct
     s_p, c_p = torch.sin(D), torch.cos(D)
     pm = []
     pv = []
-    m = torch.eye(3, dtype=F64).expand(b, 3, 3)
-    v = torch.zeros(b, 3, dtype=F64)
+    m = torch.eye(3, dtype=F64, device=dev).expand(b, 3, 3)
+    v = torch.zeros(b, 3, dtype=F64, device=dev)
     for k in range(steps):
         r, t = local_transform64(L[:, k + 2], s_t[:, k], c_t[:, k], s_p[:, k], c_p[:, k])
         v = v + (m @ t[:, :, None])[:, :, 0]
@@ -219,9 +224,9 @@ def block_backward64(lengths, angles, dihedrals, grad_xyz, p0=None, first_direct
     dL = torch.zeros_like(L)
     dA = torch.zeros_like(A)
     dD = torch.zeros_like(D)
-    sm = torch.zeros(b, 3, 3, dtype=F64)
-    sv = torch.zeros(b, 3, dtype=F64)
-    eye = torch.eye(3, dtype=F64).expand(b, 3, 3)
+    sm = torch.zeros(b, 3, 3, dtype=F64, device=dev)
+    sv = torch.zeros(b, 3, dtype=F64, device=dev)
+    eye = torch.eye(3, dtype=F64, device=dev).expand(b, 3, 3)
     for k in range(steps - 1, -1, -1):
         tail = (frame.transpose(1, 2) @ g[:, k + 3, :, None])[:, :, 0]  # transpose_mul(frame, grad)
         sm = sm + tail[:, :, None] * pv[k][:, None, :]  # outer(tail, curr.v)
@@ -282,16 +287,16 @@ def normalize_pairs64(raw):
     return rs * inv, rc * inv, n2
 
 
-def _torsion_tiles(bond_lengths, bond_angles, b, steps):
+def _torsion_tiles(bond_lengths, bond_angles, b, steps, device="cpu"):
     lengths, sincos = torsion_constants(bond_lengths, bond_angles)
-    k = torch.arange(steps)
+    k = torch.arange(steps, device=device)
     # step k uses length phase (k+2)%3 and angle phase (k+1)%3 (torsion.cu:67-73, 219-236)
-    L = torch.tensor(lengths, dtype=F64)[(k + 2) % 3].expand(b, steps)
-    st = torch.tensor([sc[0] for sc in sincos], dtype=F64)[(k + 1) % 3].expand(b, steps)
-    ct = torch.tensor([sc[1] for sc in sincos], dtype=F64)[(k + 1) % 3].expand(b, steps)
-    l0 = torch.full((b,), lengths[0], dtype=F64)
-    l1 = torch.full((b,), lengths[1], dtype=F64)
-    a0 = torch.full((b,), float(bond_angles[0]), dtype=F64)
+    L = torch.tensor(lengths, dtype=F64, device=device)[(k + 2) % 3].expand(b, steps)
+    st = torch.tensor([sc[0] for sc in sincos], dtype=F64, device=device)[(k + 1) % 3].expand(b, steps)
+    ct = torch.tensor([sc[1] for sc in sincos], dtype=F64, device=device)[(k + 1) % 3].expand(b, steps)
+    l0 = torch.full((b,), lengths[0], dtype=F64, device=device)
+    l1 = torch.full((b,), lengths[1], dtype=F64, device=device)
+    a0 = torch.full((b,), float(bond_angles[0]), dtype=F64, device=device)
     return L, st, ct, l0, l1, a0, sincos
 
 
@@ -304,8 +309,7 @@ def torsion64(raw, bond_lengths, bond_angles):
     b, width = raw.shape
     steps = width // 2
     S, C, _ = normalize_pairs64(raw)
-    L, st, ct, l0, l1, a0, sincos = _torsion_tiles(bond_lengths, bond_angles, b, steps)
-    p0, fd, nn = _anchors(None, None, None)
+    L, st, ct, l0, l1, a0, sincos = _torsion_tiles(bond_lengths, bond_angles, b, steps, raw.device)
     # make_default_base_frame uses the constant sin/cos of angle 0, not sin(a0) recomputed.
     xyz = _torsion_nerf(L, st, ct, S, C, l0, l1, sincos[0])
     return xyz
@@ -313,15 +317,16 @@ def torsion64(raw, bond_lengths, bond_angles):
 
 def _torsion_nerf(L, st, ct, S, C, l0, l1, sc0):
     b, steps = L.shape
+    dev = L.device
     s0, c0 = sc0
-    dir1 = torch.tensor([-c0, s0, 0.0], dtype=F64)
-    side = torch.tensor([-s0, -c0, 0.0], dtype=F64)
-    frame = torch.stack([dir1, side, torch.tensor([0.0, 0.0, 1.0], dtype=F64)], -1).expand(b, 3, 3)
+    dir1 = torch.tensor([-c0, s0, 0.0], dtype=F64, device=dev)
+    side = torch.tensor([-s0, -c0, 0.0], dtype=F64, device=dev)
+    frame = torch.stack([dir1, side, torch.tensor([0.0, 0.0, 1.0], dtype=F64, device=dev)], -1).expand(b, 3, 3)
     p1 = torch.stack([l0, torch.zeros_like(l0), torch.zeros_like(l0)], -1)
     p2 = torch.stack([l0 - l1 * c0, l1 * s0, torch.zeros_like(l0)], -1)
-    m = torch.eye(3, dtype=F64).expand(b, 3, 3)
-    v = torch.zeros(b, 3, dtype=F64)
-    pts = [torch.zeros(b, 3, dtype=F64), p1, p2]
+    m = torch.eye(3, dtype=F64, device=dev).expand(b, 3, 3)
+    v = torch.zeros(b, 3, dtype=F64, device=dev)
+    pts = [torch.zeros(b, 3, dtype=F64, device=dev), p1, p2]
     for k in range(steps):
         r, t = local_transform64(L[:, k], st[:, k], ct[:, k], S[:, k], C[:, k])
         v = v + (m @ t[:, :, None])[:, :, 0]
@@ -342,21 +347,21 @@ def torsion64_with_grads(raw, grad_xyz, bond_lengths, bond_angles):
     b, width = raw.shape
     steps = width // 2
     S, C, n2 = normalize_pairs64(raw)
-    L, st, ct, l0, l1, a0, sincos = _torsion_tiles(bond_lengths, bond_angles, b, steps)
+    L, st, ct, l0, l1, a0, sincos = _torsion_tiles(bond_lengths, bond_angles, b, steps, raw.device)
     xyz = _torsion_nerf(L, st, ct, S, C, l0, l1, sincos[0])
     g = grad_xyz.to(F64)
     lengths, _ = torsion_constants(bond_lengths, bond_angles)
     force = torch.flip(torch.cumsum(torch.flip(g, [1]), 1), [1])  # force[:, j] = sum_{i>=j} g_i
     moment = torch.flip(torch.cumsum(torch.flip(torch.linalg.cross(xyz, g, dim=-1), [1]), 1), [1])
-    k = torch.arange(steps)
+    k = torch.arange(steps, device=raw.device)
     prev, pivot = xyz[:, k + 1], xyz[:, k + 2]
     Fk, Mk = force[:, k + 3], moment[:, k + 3]
-    inv_len = 1.0 / torch.tensor(lengths, dtype=F64)[(k + 1) % 3]
+    inv_len = 1.0 / torch.tensor(lengths, dtype=F64, device=raw.device)[(k + 1) % 3]
     tau = Mk - torch.linalg.cross(pivot, Fk, dim=-1)
     dphi = inv_len * ((pivot - prev) * tau).sum(-1)
     rs = raw[:, 0::2].to(F64)
     rc = raw[:, 1::2].to(F64)
-    grad = torch.empty(b, width, dtype=F64)
+    grad = torch.empty(b, width, dtype=F64, device=raw.device)
     grad[:, 0::2] = dphi * rc / n2
     grad[:, 1::2] = -dphi * rs / n2
     return xyz, grad
