@@ -173,3 +173,38 @@ def test_raw_op_checks():
         C.block_backward_from_xyz32(L, A, D, None, None, None, xyz32[:, :-1].contiguous(), G)
     with pytest.raises(RuntimeError, match="supports float16 and bfloat16"):
         C.block_forward_xyz32(L.float(), A.float(), D.float())
+
+
+@pytest.mark.parametrize("dtype_code,dtype", [(2, torch.float16), (3, torch.bfloat16)])
+@pytest.mark.parametrize("xyz_shift,xyz32_shift", [(0, 0), (1, 0), (0, 1), (3, 2)])
+def test_c_abi_offset_rows_take_the_element_paths(dtype_code, dtype, xyz_shift, xyz32_shift):
+    # xyz and xyz32 rows whose residues mod 16 do not pair up (buffers shifted by whole elements):
+    # the 16-bit output row and the grad row then move element by element; results stay within
+    # the 16-bit tolerances of the oracle
+    lib = ctypes.CDLL(str(_native.LIB_PATH))
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_block_forward_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    lib.cufkb_block_backward_from_xyz32.argtypes = [ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+    B, N = 21, 301
+    inp = nerf64.make_inputs(B, N, seed=8)
+    L, A, D, G, _ = _cuda(inp, dtype, False)
+    xyz_buf = torch.zeros(B * N * 3 + 8, device="cuda", dtype=dtype)
+    xyz32_buf = torch.zeros(B * N * 3 + 8, device="cuda", dtype=torch.float32)
+    xyz = xyz_buf[xyz_shift : xyz_shift + B * N * 3].view(B, N, 3)
+    xyz32 = xyz32_buf[xyz32_shift : xyz32_shift + B * N * 3].view(B, N, 3)
+    stream = torch.cuda.current_stream().cuda_stream
+    st = lib.cufkb_block_forward_xyz32(dtype_code, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, xyz.data_ptr(), xyz32.data_ptr(), B, N, stream)
+    assert st == 0
+    got = [torch.full_like(t, float("nan")) for t in (L, A, D)]
+    st = lib.cufkb_block_backward_from_xyz32(dtype_code, L.data_ptr(), A.data_ptr(), D.data_ptr(), None, None, None, xyz32.data_ptr(), G.data_ptr(),
+                                             *(t.data_ptr() for t in got), B, N, stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    # the buffers around the rows are untouched
+    assert not xyz_buf[:xyz_shift].any() and not xyz_buf[xyz_shift + B * N * 3 :].any()
+    assert not xyz32_buf[:xyz32_shift].any() and not xyz32_buf[xyz32_shift + B * N * 3 :].any()
+    assert torch.equal(xyz, xyz32.to(dtype))
+    ref = _oracle(inp, dtype, False)
+    assert float((xyz32.double().cpu() - ref[0]).abs().max()) <= 2e-6 * max(1.0, float(ref[0].abs().max())) * math.sqrt(N)
+    for a, want in zip(got, ref[1:]):
+        assert _rel(a, want) <= GTOL[dtype]
