@@ -230,6 +230,39 @@ struct LaunchEnv {
   Plan plan;
 };
 
+// Grids of at most this many CTAs per SM are launched with programmatic dependent launch.  Every
+// kernel of this library lets the next kernel in the stream be scheduled as soon as all of its CTAs
+// have started (enter_after_previous_grid); for a small grid that hides the launch latency between
+// the two (B200, config-1 chains, forward + backward per step: 512 chains 12.5 -> 11.5 us, 1024
+// chains 16.5 -> 15.5 us), but the next kernel's CTAs, resident early and waiting, slowed larger
+// ones (2048 chains: 26.8 -> 29.1 us), which therefore launch plainly.
+constexpr int kOverlapCtasPerSm = 8;
+
+// Launches `kernel` on `stream`; small grids (kOverlapCtasPerSm) allow programmatic dependent launch:
+// the kernel may then be scheduled while the previous kernel in the stream finishes, and, like every
+// kernel of this library, waits for that kernel's completion (enter_after_previous_grid) before
+// touching global memory.  Returns the launch's own error.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  int dev = 0, sms = 148;
+  if (current_device(&dev) == 0) {
+    const DeviceCache* d = device_cache(dev);
+    if (!d->error) sms = d->sm_count;
+  }
+  const uint64_t ctas = uint64_t(grid.x) * grid.y * grid.z;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = ctas <= uint64_t(kOverlapCtasPerSm) * sms ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Device, kernel footprint, shared-memory opt-in and plan of one launch.
 template <typename Kernel>
 int launch_env(LaunchEnv* env, Kernel kernel, int kernel_id, int64_t batch, int points, size_t smem, int target = kTargetWarpsPerSm,
@@ -445,8 +478,7 @@ int launch_vec(int64_t batch, int points, int items, cudaStream_t stream, Args..
   const size_t smem = vec_smem<F, T>(points, items);
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(vec_kind(F, W), dtype_index<T>()), batch, points, smem)) return st;
-  kernel<<<static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream>>>(args...);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream, args...)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -461,7 +493,8 @@ int block_forward_vec(const void* L, const void* A, const void* D, const void* p
                       cudaStream_t stream, cufkb::PackedLayout packed) {
   const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
   const int delta = vec_delta_max<T>(xyz, points, packed.offsets != nullptr);
-  const auto [w, items] = vec_plan<kVecForwardFamily, T>(batch, points, delta);
+  const std::pair<int, int> plan = vec_plan<kVecForwardFamily, T>(batch, points, delta);
+  const int w = plan.first, items = plan.second;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
   return with_vec_warps(w, [&](auto wc) {
     return launch_vec<kVecForwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
@@ -473,7 +506,8 @@ int block_backward_xyz_vec(const void* L, const void* A, const void* D, const vo
                            void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
   const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
   const int delta = vec_delta_max<T>(xyz, points, packed.offsets != nullptr);
-  const auto [w, items] = vec_plan<kVecBackwardFamily, T>(batch, points, delta);
+  const std::pair<int, int> plan = vec_plan<kVecBackwardFamily, T>(batch, points, delta);
+  const int w = plan.first, items = plan.second;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
   return with_vec_warps(w, [&](auto wc) {
     return launch_vec<kVecBackwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, static_cast<const T*>(xyz), static_cast<const T*>(g),
@@ -487,7 +521,8 @@ int block_backward_xyz32_impl(const void* L, const void* A, const void* D, const
                               const void* g, void* gL, void* gA, void* gD, int64_t batch, int points, cudaStream_t stream, cufkb::PackedLayout packed) {
   const cufkb::BlockArgs<T> args = block_args<T>(L, A, D, p0, fd, nn);
   const int delta = vec_delta_max<float>(xyz32, points, packed.offsets != nullptr);
-  const auto [w, items] = vec_plan<kXyz32BackwardFamily, T>(batch, points, delta);
+  const std::pair<int, int> plan = vec_plan<kXyz32BackwardFamily, T>(batch, points, delta);
+  const int w = plan.first, items = plan.second;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
   return with_vec_warps(w, [&](auto wc) {
     return launch_vec<kXyz32BackwardFamily, T, decltype(wc)::value>(batch, points, items, stream, args, xyz32, static_cast<const T*>(g),
@@ -516,8 +551,7 @@ int block_forward_impl(const void* L, const void* A, const void* D, const void* 
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<T*>(xyz), geo, xyz32);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, args, static_cast<T*>(xyz), geo, xyz32)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -531,9 +565,8 @@ int block_backward_impl(const void* L, const void* A, const void* D, const void*
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
-                                                                          static_cast<T*>(gD), geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, args, static_cast<const T*>(g), static_cast<T*>(gL), static_cast<T*>(gA),
+                                                                          static_cast<T*>(gD), geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -555,9 +588,8 @@ int block_backward_xyz_impl(const void* L, const void* A, const void* D, const v
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items, packed_layout};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
-                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, args, static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -573,9 +605,8 @@ int block_mse_impl(const void* L, const void* A, const void* D, const void* p0, 
   cufkb::BlockArgs<T> args{static_cast<const T*>(L),  static_cast<const T*>(A),  static_cast<const T*>(D),
                            static_cast<const T*>(p0), static_cast<const T*>(fd), static_cast<const T*>(nn)};
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(args, static_cast<const T*>(target), static_cast<T*>(loss), static_cast<T*>(gL),
-                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, args, static_cast<const T*>(target), static_cast<T*>(loss), static_cast<T*>(gL),
+                                                                          static_cast<T*>(gA), static_cast<T*>(gD), geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -598,9 +629,8 @@ int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsio
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kTorsionForward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTorsionTargetWarpsPerSm))) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c), static_cast<T*>(xyz),
-                                                                          geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c), static_cast<T*>(xyz),
+                                                                          geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -613,9 +643,8 @@ int torsion_backward_impl(const void* raw, int64_t raw_stride, const cufkb_torsi
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTorsionTargetWarpsPerSm))) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
-                                                                          static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+                                                                          static_cast<const T*>(g), static_cast<T*>(graw), grad_stride, geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -629,10 +658,9 @@ int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_t
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kTorsionBackwardXyz, dtype_index<T>()), batch, points, smem, kTorsionTargetWarpsPerSm)) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch), env.plan.threads, smem, stream>>>(static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c),
                                                                           static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(graw),
-                                                                          grad_stride, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+                                                                          grad_stride, geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -661,8 +689,7 @@ int long_totals_launch(const cufkb::BlockArgs<T>& args, typename cufkb::ComputeO
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kLongTotals, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
   const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream, args, totals, geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -670,8 +697,7 @@ int long_totals_launch(const cufkb::BlockArgs<T>& args, typename cufkb::ComputeO
 template <typename R>
 int long_scan_launch(R* totals, R* sums, int64_t batch, const LongPlan& lp, cudaStream_t stream) {
   constexpr int kThreads = 128;
-  cufkb::long_scan_kernel<R><<<ceil_div(batch, kThreads), kThreads, 0, stream>>>(totals, sums, static_cast<int>(batch), lp.segs);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(cufkb::long_scan_kernel<R>, static_cast<unsigned>(ceil_div(batch, kThreads)), kThreads, 0, stream, totals, sums, static_cast<int>(batch), lp.segs)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -687,8 +713,7 @@ int block_forward_long_impl(const cufkb::BlockArgs<T>& args, void* xyz, int64_t 
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kLongForward, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
   const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, static_cast<T*>(xyz), geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream, args, totals, static_cast<T*>(xyz), geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -705,8 +730,7 @@ int block_backward_long_impl(const cufkb::BlockArgs<T>& args, const void* xyz, c
     LaunchEnv env;
     if (int st = launch_env(&env, kernel, kernel_id(kLongSums, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, 0)) return st;
     const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
-    kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, 0, stream>>>(static_cast<const T*>(xyz), static_cast<const T*>(g), sums, geo);
-    if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+    if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch * lp.segs), env.plan.threads, 0, stream, static_cast<const T*>(xyz), static_cast<const T*>(g), sums, geo)) return fail_cuda(e);
   }
   if (int st = long_scan_launch<R>(totals, sums, batch, lp, stream)) return st;
   const size_t smem = cufkb::long_smem_bytes<T>(lp.seg_steps, true);
@@ -714,9 +738,8 @@ int block_backward_long_impl(const cufkb::BlockArgs<T>& args, const void* xyz, c
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kLongBackward, dtype_index<T>()), batch * lp.segs, lp.seg_steps + 3, smem)) return st;
   const cufkb::LongGeometry geo{static_cast<int>(batch), static_cast<int>(points), static_cast<int>(points - 3), lp.segs, lp.seg_steps, env.plan.items};
-  kernel<<<static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream>>>(args, totals, sums, static_cast<const T*>(g), static_cast<T*>(gL),
-                                                                                    static_cast<T*>(gA), static_cast<T*>(gD), geo);
-  if (cudaError_t e = cudaGetLastError()) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch * lp.segs), env.plan.threads, smem, stream, args, totals, sums, static_cast<const T*>(g), static_cast<T*>(gL),
+                                                                                    static_cast<T*>(gA), static_cast<T*>(gD), geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 

@@ -172,6 +172,17 @@ __device__ __forceinline__ void cp_async_wait_group() {
 }
 
 
+// Programmatic dependent launch.  The library launches small grids so that they may be scheduled
+// while the previous kernel in the stream is still running; each kernel calls this first, before any
+// global-memory access: griddepcontrol.wait returns once the previous grid has completed and its
+// writes are visible (the ordering of a plain launch; a no-op when the launch did not allow the
+// overlap), and launch_dependents then lets the next kernel in the stream be scheduled once every
+// CTA of this grid has started.  The saving is the launch latency between dependent kernels.
+__device__ __forceinline__ void enter_after_previous_grid() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 // One bulk (TMA engine) store of a 16-byte aligned, 16-byte multiple range from shared memory.

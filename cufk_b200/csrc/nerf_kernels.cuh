@@ -550,6 +550,7 @@ __device__ __forceinline__ void write_block_grads(const ChainViews<T>& cv, T* gr
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     block_forward_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo, float* __restrict__ xyz32) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
@@ -620,6 +621,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp) block_backward_kernel(BlockArgs<T> args, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
                                                                          T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -816,6 +818,7 @@ template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     block_backward_xyz_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
                               T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");
@@ -872,6 +875,7 @@ template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     block_mse_kernel(BlockArgs<T> args, const T* __restrict__ target, T* __restrict__ loss, T* __restrict__ grad_lengths, T* __restrict__ grad_angles,
                      T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the fused consumer serves 32- and 64-bit types");
@@ -1056,6 +1060,7 @@ template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_forward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts, T* __restrict__ xyz,
                            ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
@@ -1229,6 +1234,7 @@ template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_backward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
                             const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride, ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   constexpr bool kScatter = sizeof(T) >= 4;
@@ -1270,6 +1276,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_backward_xyz_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
                                 const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride,
                                 ChainGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the xyz form serves 32- and 64-bit types");

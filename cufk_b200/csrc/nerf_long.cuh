@@ -96,6 +96,7 @@ __device__ __forceinline__ Affine<V> load_total(const R* src) {
 // segment sums: sums[g] <- the sum over the segments after g.  One thread per chain.
 template <typename R>
 __global__ void long_scan_kernel(R* __restrict__ totals, R* __restrict__ sums, int batch, int segs) {
+  enter_after_previous_grid();
   const int64_t chain = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (chain >= batch) return;
   R* t = totals + chain * segs * kTotalWords;
@@ -121,6 +122,7 @@ __global__ void long_scan_kernel(R* __restrict__ totals, R* __restrict__ sums, i
 // T_g for every (chain, segment).
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp) long_totals_kernel(BlockArgs<T> args, typename ComputeOf<T>::type* __restrict__ totals, LongGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the long path serves 32- and 64-bit types");
@@ -148,6 +150,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp) long_totals_kernel(BlockArgs
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     long_forward_kernel(BlockArgs<T> args, const typename ComputeOf<T>::type* __restrict__ totals, T* __restrict__ xyz, LongGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the long path serves 32- and 64-bit types");
@@ -203,6 +206,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     long_sums_kernel(const T* __restrict__ xyz, const T* __restrict__ grad_xyz, typename ComputeOf<T>::type* __restrict__ sums, LongGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   __shared__ V red[kMaxWarps * kSumWords];
@@ -248,6 +252,7 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     long_backward_kernel(BlockArgs<T> args, const typename ComputeOf<T>::type* __restrict__ totals, const typename ComputeOf<T>::type* __restrict__ sums,
                          const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths, T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals,
                          LongGeometry geo) {
+  enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
   static_assert(sizeof(T) >= 4, "the long path serves 32- and 64-bit types");

@@ -247,6 +247,7 @@ __device__ __noinline__ Affine<V> vec_forward_redo(const BlockArgs<T>& args, con
 
 template <typename T, int W, int C>
 __global__ void __launch_bounds__(kWarp* W* C) block_forward_vec_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo) {
+  enter_after_previous_grid();
   static_assert(sizeof(T) >= 4, "vector slots hold 32- and 64-bit types");
   static_assert(C == 1 || W == 1, "several chains per CTA only with one warp per chain");
   using V = T;
@@ -447,6 +448,7 @@ template <typename T, int W>
 __global__ void __launch_bounds__(kWarp* W)
     block_backward_xyz_vec_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
                                   T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  enter_after_previous_grid();
   static_assert(sizeof(T) >= 4, "vector slots hold 32- and 64-bit types");
   using R = T;
   using V = T;
@@ -687,6 +689,7 @@ template <typename T, int W>
 __global__ void __launch_bounds__(kWarp* W)
     block_backward_xyz32_kernel(BlockArgs<T> args, const float* __restrict__ xyz32, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
                                 T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  enter_after_previous_grid();
   static_assert(sizeof(T) == 2, "the float32-position backward serves the 16-bit types");
   using V = float;
   constexpr int G = VecSlots<float>::kAtoms;
