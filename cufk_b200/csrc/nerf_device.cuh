@@ -572,6 +572,15 @@ __host__ __device__ inline ChainRows rows_at(int64_t chain, int64_t first_point,
 // [p, p + n) in [0, total), lengths [p - b, p - b + n - 1) in [0, total - B), angles
 // [p - 2b, ...) in [0, total - 2B), dihedrals [p - 3b, ...) in [0, total - 3B).  So offsets that
 // are not those of a packed layout cannot make a kernel read or write out of bounds.
+// L2 prefetch (one request to the bulk-copy engine) of the 16-byte aligned interior of a global
+// row.  A prefetch only warms L2, the GPU's point of coherence, so it is safe before the previous
+// kernel has finished: a value that kernel writes afterwards is what the later loads see.
+__device__ __forceinline__ void prefetch_row_l2(const void* p, size_t bytes) {
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15u) & ~uintptr_t(15);
+  const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+  if (e > a) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a), "r"(static_cast<uint32_t>(e - a)) : "memory");
+}
+
 __device__ __forceinline__ ChainRows chain_rows(const ChainGeometry& g, int64_t chain) {
   if (g.packed.offsets == nullptr) return rows_at(chain, chain * g.points, g.points);
   const int64_t p0 = g.packed.offsets[chain];

@@ -49,6 +49,26 @@ struct BlockArgs {
   const T* initial_normal;   // (3,) or null = (0, 0, 1)
 };
 
+// The prefetches of a launch that overlaps the previous kernel ((B, N) batches, whose rows need no
+// offsets from memory): the chain's three input rows (forward), or two (B, N, 3) rows (xyz backward:
+// positions and grad).  Thread 0 of each chain, before it waits for the previous grid.
+template <typename T>
+__device__ __forceinline__ void prefetch_input_rows(const BlockArgs<T>& args, const ChainGeometry& g, int64_t chain) {
+  if (chain >= g.batch) return;
+  const ChainRows r = chain_rows(g, chain);
+  prefetch_row_l2(args.lengths + r.lengths, sizeof(T) * (r.points - 1));
+  prefetch_row_l2(args.angles + r.angles, sizeof(T) * (r.points - 2));
+  prefetch_row_l2(args.dihedrals + r.dihedrals, sizeof(T) * (r.points - 3));
+}
+
+template <typename A, typename B>
+__device__ __forceinline__ void prefetch_point_rows(const A* rows_a, const B* rows_b, const ChainGeometry& g, int64_t chain) {
+  if (chain >= g.batch) return;
+  const ChainRows r = chain_rows(g, chain);
+  prefetch_row_l2(rows_a + r.xyz, sizeof(A) * 3 * r.points);
+  prefetch_row_l2(rows_b + r.xyz, sizeof(B) * 3 * r.points);
+}
+
 template <typename R>
 struct TorsionConsts {
   R length[3];  // bond lengths by phase, rounded to float first (torsion.cu:43-47)

@@ -245,8 +245,15 @@ __device__ __noinline__ Affine<V> vec_forward_redo(const BlockArgs<T>& args, con
   return P;
 }
 
-template <typename T, int W, int C>
+// kPrefetch: the instantiation for launches that overlap the previous kernel ((B, N) batches); its
+// chains' rows are asked of L2 before the grid dependency wait.  A separate instantiation because
+// the prefetch code, even untaken, measured slower in large plain launches (config 1: 47.6 against
+// 47.3 us per step).
+template <typename T, int W, int C, bool kPrefetch = false>
 __global__ void __launch_bounds__(kWarp* W* C) block_forward_vec_kernel(BlockArgs<T> args, T* __restrict__ xyz, ChainGeometry geo) {
+  if constexpr (kPrefetch) {
+    if (threadIdx.x % (kWarp * W) == 0) prefetch_input_rows(args, geo, int64_t(blockIdx.x) * C + threadIdx.x / (kWarp * W));
+  }
   enter_after_previous_grid();
   static_assert(sizeof(T) >= 4, "vector slots hold 32- and 64-bit types");
   static_assert(C == 1 || W == 1, "several chains per CTA only with one warp per chain");
@@ -444,10 +451,13 @@ struct VecBackwardShared {
   V g12[6];  // incoming gradients of atoms 1 and 2
 };
 
-template <typename T, int W>
+template <typename T, int W, bool kPrefetch = false>
 __global__ void __launch_bounds__(kWarp* W)
     block_backward_xyz_vec_kernel(BlockArgs<T> args, const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_lengths,
                                   T* __restrict__ grad_angles, T* __restrict__ grad_dihedrals, ChainGeometry geo) {
+  if constexpr (kPrefetch) {
+    if (threadIdx.x == 0) prefetch_point_rows(xyz, grad_xyz, geo, blockIdx.x);  // as block_forward_vec_kernel's
+  }
   enter_after_previous_grid();
   static_assert(sizeof(T) >= 4, "vector slots hold 32- and 64-bit types");
   using R = T;
