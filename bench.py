@@ -840,7 +840,7 @@ def run_workload(args, dist: Dist) -> dict:
         names = ("block_mse_kernel", None)
     else:
         fwd_b, bwd_b = (2 * steps_s + 3 * points) * elem, (4 * steps_s + 3 * points) * elem
-        names = ("torsion_forward_kernel", "torsion_backward_xyz_kernel" if elem >= 4 else "torsion_backward_kernel")
+        names = ("torsion_forward_kernel", "torsion_backward_xyz_vec_kernel" if elem >= 4 else "torsion_backward_kernel")
     set_bytes = b_local * (fwd_b + bwd_b)
     n_sets = max(2, min(16, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
     consts = torsion_constants(BACKBONE_LENGTHS, BACKBONE_ANGLES)

@@ -25,7 +25,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 124;  // kKindCount x 4 dtypes
+constexpr int kNumKernels = 140;  // kKindCount x 4 dtypes
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -313,7 +313,7 @@ enum KernelKind {
   kBlockMse = 10,
   // vector-slot kernels: kVecKindBase + family x warp count (vec_kind)
   kVecKindBase = 11,
-  kKindCount = 31
+  kKindCount = 35
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
@@ -403,9 +403,16 @@ int with_vec_warps(int w, F&& f) {
 }
 
 // The *Prefetch families are the instantiations for launches that overlap the previous kernel.
-enum VecFamily { kVecForwardFamily = 0, kVecBackwardFamily = 1, kXyz32BackwardFamily = 2, kVecForwardPrefetchFamily = 3, kVecBackwardPrefetchFamily = 4 };
+enum VecFamily {
+  kVecForwardFamily = 0,
+  kVecBackwardFamily = 1,
+  kXyz32BackwardFamily = 2,
+  kVecForwardPrefetchFamily = 3,
+  kVecBackwardPrefetchFamily = 4,
+  kTorsionBackwardFamily = 5
+};
 constexpr KernelKind vec_kind(VecFamily f, int w) { return static_cast<KernelKind>(kVecKindBase + f * kNumVecWarpCounts + vec_warp_slot(w)); }
-static_assert(kVecKindBase + 5 * kNumVecWarpCounts == kKindCount, "kind table");
+static_assert(kVecKindBase + 6 * kNumVecWarpCounts == kKindCount, "kind table");
 
 // Warps per chain of a vector kernel whose slots hold `Elem`: the fewest with at most
 // CUFKB_VEC_MAX_GROUPS groups of G atoms per thread, then twice as many while the SM would hold
@@ -449,6 +456,10 @@ auto vec_kernel(std::integral_constant<VecFamily, kVecBackwardFamily>) {
   return cufkb::block_backward_xyz_vec_kernel<T, W>;
 }
 template <typename T, int W>
+auto vec_kernel(std::integral_constant<VecFamily, kTorsionBackwardFamily>) {
+  return cufkb::torsion_backward_xyz_vec_kernel<T, W>;
+}
+template <typename T, int W>
 auto vec_kernel(std::integral_constant<VecFamily, kVecForwardPrefetchFamily>) {
   return cufkb::block_forward_vec_kernel<T, W, 1, true>;
 }
@@ -466,6 +477,9 @@ template <VecFamily F, typename T>
 size_t vec_smem(int points, int items) {
   if constexpr (F == kVecForwardFamily || F == kVecForwardPrefetchFamily) return cufkb::vec_row_bytes(points, items, sizeof(T));
   if constexpr (F == kVecBackwardFamily || F == kVecBackwardPrefetchFamily) return 2 * cufkb::vec_row_bytes(points, items, sizeof(T));
+  if constexpr (F == kTorsionBackwardFamily) {
+    return 2 * cufkb::vec_row_bytes(points, items, sizeof(T)) + cufkb::staged_row_bytes(size_t(2) * (points - 3), sizeof(T));
+  }
   return cufkb::xyz32_pos_region_bytes<T>(points, items) + cufkb::xyz32_grad_region_bytes<T>(points, items);
 }
 
@@ -679,6 +693,18 @@ template <typename T>
 int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const void* xyz, const void* g, void* graw,
                               int64_t grad_stride, int64_t batch, int points, cudaStream_t stream) {
   using R = typename cufkb::ComputeOf<T>::type;
+  // the vector form stages xyz and grad rows with one shift: their rows must share the residue mod 16
+  if ((reinterpret_cast<uintptr_t>(xyz) - reinterpret_cast<uintptr_t>(g)) % 16 == 0) {
+    const int delta = vec_delta_max<T>(xyz, points, false);
+    const std::pair<int, int> plan = vec_plan<kTorsionBackwardFamily, T>(batch, points, delta);
+    const int w = plan.first, items = plan.second;
+    const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items};
+    return with_vec_warps(w, [&](auto wc) {
+      return launch_vec<kTorsionBackwardFamily, T, decltype(wc)::value>(batch, points, items, stream, static_cast<const T*>(raw), raw_stride,
+                                                                         torsion_consts<R>(c), static_cast<const T*>(xyz), static_cast<const T*>(g),
+                                                                         static_cast<T*>(graw), grad_stride, geo);
+    });
+  }
   const size_t smem = cufkb::torsion_xyz_smem_bytes<T>(points);
   auto kernel = cufkb::torsion_backward_xyz_kernel<T>;
   LaunchEnv env;

@@ -6,6 +6,8 @@
 //                                      (float32, float64)
 //   block_backward_xyz32_kernel       the gradients of block.cu:206-313 for float16/bfloat16 from
 //                                      the float32 positions block_forward_kernel writes beside xyz
+//   torsion_backward_xyz_vec_kernel   the raw-pair gradients of torsion.cu:297-381 from the forward's
+//                                      xyz (float32, float64)
 //
 // They compute what block_forward_kernel and block_backward_xyz_kernel compute, with fewer
 // instructions per atom:
@@ -656,6 +658,190 @@ __global__ void __launch_bounds__(kWarp* W)
 // --------------------------------------------------------------------------------------------
 // 16-bit backward from float32 positions
 // --------------------------------------------------------------------------------------------
+// The torsion xyz backward (torsion_backward_xyz_kernel's algorithm, the reference's own form
+// torsion.cu:297-381 for the raw-pair gradients) in vector slots, as block_backward_xyz_vec_kernel
+// runs the block one: positions and grad in two shifted slot rows, the sums of g and (x - o) x g
+// per thread, the exclusive suffix scan, then one sweep giving d phi of each step, with the torque
+// about the previous atom carried from step to step.  The raw row, staged beside them (reading it
+// from global memory at the end instead measured 126 against 105 us at config 3), gives the chain
+// rule to the (sin, cos) pairs.  Chains with a bond shorter than 1e-3 |x|max, or a pair below the
+// norm clamp, take the recompute form in the same CTA.
+template <typename T, int W>
+__global__ void __launch_bounds__(kWarp* W)
+    torsion_backward_xyz_vec_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts,
+                                    const T* __restrict__ xyz, const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride,
+                                    ChainGeometry geo) {
+  enter_after_previous_grid();
+  static_assert(sizeof(T) >= 4, "vector slots hold 32- and 64-bit types");
+  using R = T;
+  using V = T;
+  constexpr int G = VecSlots<T>::kAtoms;
+  constexpr int NT = kWarp * W;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ VecChainShared<V, W> sh;
+  __shared__ CtaExchange<V> ex;  // the recompute form's scans
+
+  const int u = static_cast<int>(threadIdx.x);
+  const int64_t chain = blockIdx.x;
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const T* raw = raw_pairs + chain * raw_stride;
+  const T* xrow = xyz + chain * 3 * N;
+  const T* grow = grad_xyz + chain * 3 * N;
+  const uintptr_t residue = reinterpret_cast<uintptr_t>(xrow) & 15u;  // the host checked grad's equals it
+  const int delta = vec_delta<T>(residue);
+  const size_t row_bytes = vec_row_bytes(N, K, sizeof(T));
+  unsigned char* const xregion = smem;
+  unsigned char* const gregion = smem + row_bytes;
+  unsigned char* const rregion = smem + 2 * row_bytes;
+  T* const X = reinterpret_cast<T*>(xregion + kVecFrontPad + residue);
+  T* const Gd = reinterpret_cast<T*>(gregion + kVecFrontPad + residue);
+  const int live = (N + delta + K - 1) / K;
+  const int a0 = u * K - delta;
+  const int pad_end = live * K - delta;
+
+  stage_row_async(xregion + kVecFrontPad, xrow, 3 * N, u, NT);
+  stage_row_async(gregion + kVecFrontPad, grow, 3 * N, u, NT);
+  const T* raw_s = stage_row_async(rregion, raw, 2 * St, u, NT);
+  for (int i = u; i < 15; i += NT) Gd[i - 15] = T(0);
+  for (int i = 3 * N + u; i < 3 * pad_end; i += NT) Gd[i] = T(0);
+  cp_async_wait_all();
+  chain_sync<W>();
+
+  // padding positions (thread 0: in front of atom 0, the last live thread: past atom N-1); atoms
+  // 0..2 carry no gradient (the base frame is fixed), so the sums start at atom 3
+  if (u == 0) {
+    zigzag_padding<V>(X - 3, -3, 5, X, X + 3);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) Gd[i] = T(0);
+  }
+  if (u == live - 1 && pad_end > N) zigzag_padding<V>(X + 3 * N, 3, pad_end - N, X + 3 * (N - 1), X + 3 * (N - 2));
+  const V o[3] = {X[6], X[7], X[8]};
+  // pass 1: the thread's sums of g and (x - o) x g, and its largest |x|^2
+  V gsum[3] = {V(0), V(0), V(0)};
+  V msum[3] = {V(0), V(0), V(0)};
+  V xmax2 = V(0);
+  const int groups = K / G;
+  if (u < live) {
+    const T* px = X + 3 * a0;
+    const T* pg = Gd + 3 * a0;
+#pragma unroll 1
+    for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+      SlotGroup<T> xs, gs;
+      load_group(px, xs);
+      load_group(pg, gs);
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const V xw[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+        const V gg[3] = {gs.v[3 * j], gs.v[3 * j + 1], gs.v[3 * j + 2]};
+        xmax2 = fmax(xmax2, dot3(xw, xw));
+        const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
+        V mx[3];
+        cross3(x, gg, mx);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          gsum[i] = vadd(gsum[i], gg[i]);
+          msum[i] = vadd(msum[i], mx[i]);
+        }
+      }
+    }
+  }
+  V Fs[3], Ms[3];
+  {
+    V mine[6] = {gsum[0], gsum[1], gsum[2], msum[0], msum[1], msum[2]};
+    V after[6];
+    cta_exclusive_suffix<V, 6>(mine, after, sh.warp_sums, W);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      Fs[i] = vadd(after[i], gsum[i]);
+      Ms[i] = vadd(after[3 + i], msum[i]);
+    }
+  }
+  // pass 2: at atom a, x1 = x_{a-2}, x2 = x_{a-1} and the torque about x2,
+  // tau = sum_{j >= a} (x_j - x2) x g_j; d phi of step a-3 = (x2 - x1) . tau / |x2 - x1|; then
+  // tau <- tau - (x_a - x2) x F and F <- F - g_a.  d phi goes to word 0 of slot a.
+  V dmin2 = V(1e30);
+  if (u < live) {
+    V x1[3], x2[3], tau[3];
+    {
+      const T* q = X + 3 * (a0 - 2);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        x1[i] = q[i];
+        x2[i] = q[3 + i];
+      }
+      const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+      V xf[3];
+      cross3(xr, Fs, xf);
+#pragma unroll
+      for (int i = 0; i < 3; ++i) tau[i] = vsub(Ms[i], xf[i]);
+    }
+    const T* px = X + 3 * a0;
+    T* pg = Gd + 3 * a0;
+#pragma unroll 1
+    for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+      SlotGroup<T> xs, gs;
+      load_group(px, xs);
+      load_group(pg, gs);
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const V x3[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+        const V d[3] = {vsub(x2[0], x1[0]), vsub(x2[1], x1[1]), vsub(x2[2], x1[2])};
+        const V d2 = dot3(d, d);
+        dmin2 = fmin(dmin2, d2);
+        const V d_phi = vmul(dot3(d, tau), bond_rsqrt(d2));
+        const V e[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+        tau[0] = vfma(e[2], Fs[1], vfma(vneg(e[1]), Fs[2], tau[0]));
+        tau[1] = vfma(e[0], Fs[2], vfma(vneg(e[2]), Fs[0], tau[1]));
+        tau[2] = vfma(e[1], Fs[0], vfma(vneg(e[0]), Fs[1], tau[2]));
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          Fs[i] = vsub(Fs[i], gs.v[3 * j + i]);
+          x1[i] = x2[i];
+          x2[i] = x3[i];
+        }
+        gs.v[3 * j] = d_phi;
+      }
+      store_group(pg, gs);
+    }
+  }
+  // every bond a step uses is tested (the padding ones are sound); non-finite values fail it
+  const bool bad = u < live && !(dmin2 >= static_cast<V>(1e-6) * xmax2);
+  bool redo = chain_any<W>(bad);
+  T* gr = grad_raw + chain * grad_stride;
+  if (!redo) {
+    // chain rule, one (sin, cos) pair per thread and iteration: d raw = d phi (c, -s) / n2 with
+    // n2 = max(s^2 + c^2, clamp) (store_raw_pair_grad, torsion.cu:173-182); a pair below the norm
+    // clamp is not a rotation, and the chain is redone below
+    bool clamped = false;
+#pragma unroll 4
+    for (int k = u; k < St; k += NT) {
+      const V rs = to_r<V>(raw_s[2 * k]);
+      const V rc = to_r<V>(raw_s[2 * k + 1]);
+      const V n2raw = vfma(rs, rs, vmul(rc, rc));
+      clamped |= !(n2raw >= static_cast<V>(1.0e-8f * 1.0e-8f));
+      const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+      const V scale = vmul(Gd[3 * (k + 3)], vmul(rinv, rinv));
+      gr[2 * k] = from_r<T>(vmul(rc, scale));
+      gr[2 * k + 1] = from_r<T>(vneg(vmul(rs, scale)));
+    }
+    redo = chain_any<W>(clamped);
+  }
+  if (redo) {
+    // the recompute form, laid out as in torsion_backward_kernel
+    chain_sync<W>();
+    ChainViews<T> cv;
+    cv.X = reinterpret_cast<R*>(xregion);
+    scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, u, NT);
+    cv.G = stage_row_async(gregion, grow, 3 * N, u, NT);
+    cp_async_wait_all();
+    chain_sync<W>();
+    const StepRange range = step_range(u, (St + NT - 1) / NT, St);
+    torsion_backward_recompute<T, V, R, false>(cv, ex, consts, range, W);
+    chain_sync<W>();
+    write_pair_grads<T, R>(cv.X, gr, St, u, NT);
+  }
+}
+
 // Shared memory of block_backward_xyz32_kernel: the float32 position row (vector slots) in a region
 // that also fits the recompute form's float slots, then the 16-bit grad row with room for padding
 // atoms on both sides.
