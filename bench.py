@@ -840,7 +840,8 @@ def run_workload(args, dist: Dist) -> dict:
         names = ("block_mse_kernel", None)
     else:
         fwd_b, bwd_b = (2 * steps_s + 3 * points) * elem, (4 * steps_s + 3 * points) * elem
-        names = ("torsion_forward_kernel", "torsion_backward_xyz_vec_kernel" if elem >= 4 else "torsion_backward_kernel")
+        # the 16-bit forward also writes float32 positions, which its backward reads
+        names = ("torsion_forward_kernel", "torsion_backward_xyz_vec_kernel" if elem >= 4 else "torsion_backward_xyz32_kernel")
     set_bytes = b_local * (fwd_b + bwd_b)
     n_sets = max(2, min(16, math.ceil(3 * L2_BYTES / max(set_bytes, 1))))
     consts = torsion_constants(BACKBONE_LENGTHS, BACKBONE_ANGLES)
@@ -868,6 +869,8 @@ def run_workload(args, dist: Dist) -> dict:
             return C.block_forward_xyz32(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d))
         if kind == "block":
             return C.block_forward(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d))
+        if elem == 2:
+            return C.torsion_forward_xyz32(d["raw"], consts)
         return C.torsion_forward(d["raw"], consts)
 
     def bwd(d, xyz):
@@ -875,6 +878,8 @@ def run_workload(args, dist: Dist) -> dict:
             return C.block_backward_from_xyz32(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d), xyz[1], d["grad"])
         if kind == "block":
             return C.block_backward_from_xyz(d["lengths"], d["angles"], d["dihedrals"], *anchor_args(d), xyz, d["grad"])
+        if elem == 2:
+            return C.torsion_backward_from_xyz32(d["raw"], consts, xyz[1], d["grad"])
         return C.torsion_backward_from_xyz(d["raw"], consts, xyz, d["grad"])
 
     stream = torch.cuda.Stream()

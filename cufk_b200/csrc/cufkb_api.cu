@@ -25,7 +25,7 @@ using cufkb::ChainGeometry;
 thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumKernels = 140;  // kKindCount x 4 dtypes
+constexpr int kNumKernels = 156;  // kKindCount x 4 dtypes
 constexpr int kTargetItems = 24;  // steps per thread a long chain is split down to
 constexpr int kMinItems = 5;      // never split a chain below this many steps per thread
 // Resident warps per SM the plan aims for, per kernel.  The xyz backward aims lower: its per-thread
@@ -313,7 +313,7 @@ enum KernelKind {
   kBlockMse = 10,
   // vector-slot kernels: kVecKindBase + family x warp count (vec_kind)
   kVecKindBase = 11,
-  kKindCount = 35
+  kKindCount = 39
 };
 constexpr int kernel_id(KernelKind kind, int dtype) { return kind * 4 + dtype; }
 
@@ -409,10 +409,11 @@ enum VecFamily {
   kXyz32BackwardFamily = 2,
   kVecForwardPrefetchFamily = 3,
   kVecBackwardPrefetchFamily = 4,
-  kTorsionBackwardFamily = 5
+  kTorsionBackwardFamily = 5,
+  kTorsionXyz32Family = 6
 };
 constexpr KernelKind vec_kind(VecFamily f, int w) { return static_cast<KernelKind>(kVecKindBase + f * kNumVecWarpCounts + vec_warp_slot(w)); }
-static_assert(kVecKindBase + 6 * kNumVecWarpCounts == kKindCount, "kind table");
+static_assert(kVecKindBase + 7 * kNumVecWarpCounts == kKindCount, "kind table");
 
 // Warps per chain of a vector kernel whose slots hold `Elem`: the fewest with at most
 // CUFKB_VEC_MAX_GROUPS groups of G atoms per thread, then twice as many while the SM would hold
@@ -460,6 +461,10 @@ auto vec_kernel(std::integral_constant<VecFamily, kTorsionBackwardFamily>) {
   return cufkb::torsion_backward_xyz_vec_kernel<T, W>;
 }
 template <typename T, int W>
+auto vec_kernel(std::integral_constant<VecFamily, kTorsionXyz32Family>) {
+  return cufkb::torsion_backward_xyz32_kernel<T, W>;
+}
+template <typename T, int W>
 auto vec_kernel(std::integral_constant<VecFamily, kVecForwardPrefetchFamily>) {
   return cufkb::block_forward_vec_kernel<T, W, 1, true>;
 }
@@ -477,6 +482,7 @@ template <VecFamily F, typename T>
 size_t vec_smem(int points, int items) {
   if constexpr (F == kVecForwardFamily || F == kVecForwardPrefetchFamily) return cufkb::vec_row_bytes(points, items, sizeof(T));
   if constexpr (F == kVecBackwardFamily || F == kVecBackwardPrefetchFamily) return 2 * cufkb::vec_row_bytes(points, items, sizeof(T));
+  if constexpr (F == kTorsionXyz32Family) return cufkb::torsion_xyz32_bytes<T>(points, items);
   if constexpr (F == kTorsionBackwardFamily) {
     return 2 * cufkb::vec_row_bytes(points, items, sizeof(T)) + cufkb::staged_row_bytes(size_t(2) * (points - 3), sizeof(T));
   }
@@ -662,15 +668,18 @@ cufkb::TorsionConsts<R> torsion_consts(const cufkb_torsion_constants* c) {
 }
 
 template <typename T>
-int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points, cudaStream_t stream) {
+int torsion_forward_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, void* xyz, int64_t batch, int points, cudaStream_t stream,
+                         float* xyz32 = nullptr) {
   using R = typename cufkb::ComputeOf<T>::type;
   const size_t smem = cufkb::torsion_smem_bytes<T>(points, false);
   auto kernel = cufkb::torsion_forward_kernel<T>;
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(kTorsionForward, dtype_index<T>()), batch, points, smem, target_warps<T>(kTorsionTargetWarpsPerSm))) return st;
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, env.plan.items};
-  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, static_cast<const T*>(raw), raw_stride, torsion_consts<R>(c), static_cast<T*>(xyz),
-                                                                          geo)) return fail_cuda(e);
+  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), env.plan.threads, smem, stream, static_cast<const T*>(raw), raw_stride,
+                                    torsion_consts<R>(c), static_cast<T*>(xyz), geo, xyz32)) {
+    return fail_cuda(e);
+  }
   return CUFKB_SUCCESS;
 }
 
@@ -714,6 +723,21 @@ int torsion_backward_xyz_impl(const void* raw, int64_t raw_stride, const cufkb_t
                                                                           static_cast<const T*>(xyz), static_cast<const T*>(g), static_cast<T*>(graw),
                                                                           grad_stride, geo)) return fail_cuda(e);
   return CUFKB_SUCCESS;
+}
+
+// The 16-bit torsion backward from the torsion forward's float32 positions.
+template <typename T>
+int torsion_backward_xyz32_impl(const void* raw, int64_t raw_stride, const cufkb_torsion_constants* c, const float* xyz32, const void* g, void* graw,
+                                int64_t grad_stride, int64_t batch, int points, cudaStream_t stream) {
+  const int delta = vec_delta_max<float>(xyz32, points, false);
+  const std::pair<int, int> plan = vec_plan<kTorsionXyz32Family, T>(batch, points, delta);
+  const int w = plan.first, items = plan.second;
+  const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items};
+  return with_vec_warps(w, [&](auto wc) {
+    return launch_vec<kTorsionXyz32Family, T, decltype(wc)::value>(batch, points, items, stream, static_cast<const T*>(raw), raw_stride,
+                                                                   torsion_consts<float>(c), xyz32, static_cast<const T*>(g), static_cast<T*>(graw),
+                                                                   grad_stride, geo);
+  });
 }
 
 // ---- chains longer than one CTA: segments of at most CUFKB_MAX_STEPS steps ----
@@ -1142,6 +1166,39 @@ int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, int64_t ra
   return torsion_backward_xyz_impl<double>(raw_pairs, raw_row_stride, constants, xyz, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
 }
 
+int cufkb_torsion_forward_xyz32(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants, void* xyz,
+                                float* xyz32, int64_t batch, int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (dtype != CUFKB_FLOAT16 && dtype != CUFKB_BFLOAT16) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!raw_pairs || !xyz || !xyz32) return CUFKB_ERROR_NULL_POINTER;
+  if (!constants) return CUFKB_ERROR_INVALID_VALUE;
+  if (raw_row_stride < 0) return CUFKB_ERROR_BAD_STRIDE;
+  if (!aligned(raw_pairs, 2) || !aligned(xyz, 2) || !aligned(xyz32, sizeof(float))) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT16) return torsion_forward_impl<__half>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, xyz32);
+  return torsion_forward_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, xyz, batch, n, s, xyz32);
+}
+
+int cufkb_torsion_backward_from_xyz32(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                                      const float* xyz32, const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch,
+                                      int64_t points, cufkb_stream_t stream) {
+  if (int st = check_shape(dtype, batch, points)) return st;
+  if (dtype != CUFKB_FLOAT16 && dtype != CUFKB_BFLOAT16) return CUFKB_ERROR_UNSUPPORTED_DTYPE;
+  if (batch == 0) return CUFKB_SUCCESS;
+  if (!raw_pairs || !xyz32 || !grad_xyz || !grad_raw_pairs) return CUFKB_ERROR_NULL_POINTER;
+  if (!constants) return CUFKB_ERROR_INVALID_VALUE;
+  if (raw_row_stride < 0 || grad_row_stride < 0 || (batch > 1 && grad_row_stride < 2 * (points - 3))) return CUFKB_ERROR_BAD_STRIDE;
+  if (!aligned(raw_pairs, 2) || !aligned(xyz32, sizeof(float)) || !aligned(grad_xyz, 2) || !aligned(grad_raw_pairs, 2)) return CUFKB_ERROR_MISALIGNED;
+  const int n = static_cast<int>(points);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CUFKB_FLOAT16) {
+    return torsion_backward_xyz32_impl<__half>(raw_pairs, raw_row_stride, constants, xyz32, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
+  }
+  return torsion_backward_xyz32_impl<__nv_bfloat16>(raw_pairs, raw_row_stride, constants, xyz32, grad_xyz, grad_raw_pairs, grad_row_stride, batch, n, s);
+}
+
 int cufkb_block_long_workspace_bytes(int dtype, int64_t batch, int64_t points, size_t* bytes) {
   if (!bytes) return CUFKB_ERROR_NULL_POINTER;
   *bytes = 0;
@@ -1241,7 +1298,7 @@ const char* cufkb_status_string(int status) {
     case CUFKB_ERROR_WORKSPACE:
       return "workspace is smaller than cufkb_block_long_workspace_bytes";
     case CUFKB_ERROR_UNSUPPORTED_DTYPE:
-      return "dtype not served here: chains longer than 2051 points and the fused loss take float32 and float64 only, the float32-position entries float16 and bfloat16 only";
+      return "dtype not served here: chains longer than 2051 points and the fused loss take float32 and float64 only, the float32-position (xyz32) entries float16 and bfloat16 only";
     case CUFKB_ERROR_SCRATCH_CAPACITY:
       return "batch x segments exceeds the 2 MiB static scratch of cufkb_block_forward_long_static";
     default:

@@ -1079,7 +1079,7 @@ __device__ __forceinline__ Affine<V> torsion_sweep(const ChainViews<T>& cv, Step
 template <typename T>
 __global__ void __launch_bounds__(kMaxWarps* kWarp)
     torsion_forward_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<typename ComputeOf<T>::type> consts, T* __restrict__ xyz,
-                           ChainGeometry geo) {
+                           ChainGeometry geo, float* __restrict__ xyz32) {
   enter_after_previous_grid();
   using R = typename ComputeOf<T>::type;
   using V = R;
@@ -1097,7 +1097,8 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
     cv.X = reinterpret_cast<R*>(smem + (reinterpret_cast<uintptr_t>(out) & 15u));
     scatter_pairs<T>(reinterpret_cast<T*>(cv.X), raw, St, tid, nthr);
   } else {
-    cv.X = reinterpret_cast<R*>(smem + half_slot_residue(out, nullptr));  // lines up with out for store_half_row
+    // the float slots line up with out for store_half_row, and with xyz32's row when there is one
+    cv.X = reinterpret_cast<R*>(smem + half_slot_residue(out, xyz32 != nullptr ? xyz32 + chain * 3 * N : nullptr));
     cv.row[0] = stage_row_async(smem + slot_bytes(N, sizeof(R)), raw, 2 * St, tid, nthr);
   }
   V F[9], p1[3], p2[3];
@@ -1117,6 +1118,17 @@ __global__ void __launch_bounds__(kMaxWarps* kWarp)
   const Affine<V> total = torsion_sweep<T, V, R>(cv, range, consts);
   const Affine<V> W = world_carry(cta_exclusive_affine<V>(total, ex.warp_totals, nwarps), F, p2);
   apply_carry<T, V>(cv, W, range);
+  if constexpr (!kScatter) {
+    if (xyz32 != nullptr) {
+      // the float32 positions as well (the 16-bit xyz backward reads them)
+      fence_proxy_async_smem();
+      __syncthreads();
+      store_row_bulk<float>(xyz32 + chain * 3 * N, reinterpret_cast<const float*>(cv.X), 3 * N, tid, nthr, 0);
+      store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
+      if (tid == 0) bulk_store_wait_read();
+      return;
+    }
+  }
   store_xyz_row<T, R>(out, cv.X, N, tid, nthr);
 }
 

@@ -8,6 +8,8 @@
 //                                      the float32 positions block_forward_kernel writes beside xyz
 //   torsion_backward_xyz_vec_kernel   the raw-pair gradients of torsion.cu:297-381 from the forward's
 //                                      xyz (float32, float64)
+//   torsion_backward_xyz32_kernel     the same for float16/bfloat16 from the torsion forward's float32
+//                                      positions
 //
 // They compute what block_forward_kernel and block_backward_xyz_kernel compute, with fewer
 // instructions per atom:
@@ -1077,6 +1079,187 @@ __global__ void __launch_bounds__(kWarp* W)
     }
     chain_sync<W>();
     write_block_grads<T>(cv, grad_lengths, grad_angles, grad_dihedrals, rows, u, NT);
+  }
+}
+
+// Shared memory of torsion_backward_xyz32_kernel: float32 positions in a vector row that also fits
+// the recompute form's float slots, the 16-bit grad row (xyz32_grad_region_bytes) and the 16-bit
+// raw row.
+template <typename T>
+__host__ __device__ inline size_t torsion_xyz32_bytes(int points, int items) {
+  const size_t vec = vec_row_bytes(points, items, sizeof(float));
+  const size_t redo = slot_bytes(points, sizeof(float));
+  return (vec > redo ? vec : redo) + (kHalfFrontPad + 16 + ((3 * sizeof(T) * static_cast<size_t>(points + items) + 15) & ~size_t(15))) +
+         staged_row_bytes(size_t(2) * (points - 3), sizeof(T));
+}
+
+// The torsion xyz backward of float16/bfloat16 chains from the float32 positions the 16-bit
+// torsion forward wrote beside its output: torsion_backward_xyz_vec_kernel's algorithm on float32
+// positions in vector slots, with the 16-bit grad row staged as it is and read element by element.
+// d phi stays in float (it is multiplied into both pair gradients): it goes over word 0 of the
+// position slots, once every thread has read the two positions in front of its range.  Short bonds
+// and clamped pairs take the recompute form (torsion_backward_kernel's) in the same CTA.
+template <typename T, int W>
+__global__ void __launch_bounds__(kWarp* W)
+    torsion_backward_xyz32_kernel(const T* __restrict__ raw_pairs, int64_t raw_stride, TorsionConsts<float> consts, const float* __restrict__ xyz32,
+                                  const T* __restrict__ grad_xyz, T* __restrict__ grad_raw, int64_t grad_stride, ChainGeometry geo) {
+  enter_after_previous_grid();
+  static_assert(sizeof(T) == 2, "the float32-position backward serves the 16-bit types");
+  using R = float;
+  using V = float;
+  constexpr int G = VecSlots<float>::kAtoms;
+  constexpr int NT = kWarp * W;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ VecChainShared<V, W> sh;
+  __shared__ CtaExchange<V> ex;  // the recompute form's scans
+
+  const int u = static_cast<int>(threadIdx.x);
+  const int64_t chain = blockIdx.x;
+  const int N = geo.points, St = geo.steps, K = geo.items;
+  const T* raw = raw_pairs + chain * raw_stride;
+  const float* xrow = xyz32 + chain * 3 * N;
+  const T* grow = grad_xyz + chain * 3 * N;
+  const uintptr_t residue = reinterpret_cast<uintptr_t>(xrow) & 15u;
+  const int delta = vec_delta<float>(residue);
+  const size_t vec = vec_row_bytes(N, K, sizeof(float));
+  const size_t xbytes = vec > slot_bytes(N, sizeof(float)) ? vec : slot_bytes(N, sizeof(float));
+  unsigned char* const xregion = smem;
+  unsigned char* const gregion = smem + xbytes;
+  unsigned char* const rregion = gregion + kHalfFrontPad + 16 + ((3 * sizeof(T) * static_cast<size_t>(N + K) + 15) & ~size_t(15));
+  float* const X = reinterpret_cast<float*>(xregion + kVecFrontPad + residue);
+  const int live = (N + delta + K - 1) / K;
+  const int a0 = u * K - delta;
+  const int pad_end = live * K - delta;
+
+  stage_row_async(xregion + kVecFrontPad, xrow, 3 * N, u, NT);
+  T* const Gh = stage_row_async(gregion + kHalfFrontPad, grow, 3 * N, u, NT);
+  const T* raw_s = stage_row_async(rregion, raw, 2 * St, u, NT);
+  for (int i = u; i < 15; i += NT) Gh[i - 15] = from_r<T>(0.0f);
+  for (int i = 3 * N + u; i < 3 * pad_end; i += NT) Gh[i] = from_r<T>(0.0f);
+  cp_async_wait_all();
+  chain_sync<W>();
+
+  if (u == 0) {
+    zigzag_padding<V>(X - 3, -3, 5, X, X + 3);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) Gh[i] = from_r<T>(0.0f);
+  }
+  if (u == live - 1 && pad_end > N) zigzag_padding<V>(X + 3 * N, 3, pad_end - N, X + 3 * (N - 1), X + 3 * (N - 2));
+  const V o[3] = {X[6], X[7], X[8]};
+  V gsum[3] = {V(0), V(0), V(0)};
+  V msum[3] = {V(0), V(0), V(0)};
+  V xmax2 = V(0);
+  const int groups = K / G;
+  if (u < live) {
+    const float* px = X + 3 * a0;
+    const T* pg = Gh + 3 * a0;
+#pragma unroll 1
+    for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+      SlotGroup<float> xs;
+      load_group(px, xs);
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const V xw[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+        const V gg[3] = {to_r<V>(pg[3 * j]), to_r<V>(pg[3 * j + 1]), to_r<V>(pg[3 * j + 2])};
+        xmax2 = fmax(xmax2, dot3(xw, xw));
+        const V x[3] = {vsub(xw[0], o[0]), vsub(xw[1], o[1]), vsub(xw[2], o[2])};
+        V mx[3];
+        cross3(x, gg, mx);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          gsum[i] = vadd(gsum[i], gg[i]);
+          msum[i] = vadd(msum[i], mx[i]);
+        }
+      }
+    }
+  }
+  V Fs[3], Ms[3];
+  {
+    V mine[6] = {gsum[0], gsum[1], gsum[2], msum[0], msum[1], msum[2]};
+    V after[6];
+    cta_exclusive_suffix<V, 6>(mine, after, sh.warp_sums, W);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      Fs[i] = vadd(after[i], gsum[i]);
+      Ms[i] = vadd(after[3 + i], msum[i]);
+    }
+  }
+  V dmin2 = V(1e30);
+  V x1[3], x2[3], tau[3];
+  if (u < live) {
+    const float* q = X + 3 * (a0 - 2);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      x1[i] = q[i];
+      x2[i] = q[3 + i];
+    }
+    const V xr[3] = {vsub(x2[0], o[0]), vsub(x2[1], o[1]), vsub(x2[2], o[2])};
+    V xf[3];
+    cross3(xr, Fs, xf);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) tau[i] = vsub(Ms[i], xf[i]);
+  }
+  chain_sync<W>();  // d phi goes over the position slots: every thread has read its two in front
+  if (u < live) {
+    float* px = X + 3 * a0;
+    const T* pg = Gh + 3 * a0;
+#pragma unroll 1
+    for (int g = 0; g < groups; ++g, px += 3 * G, pg += 3 * G) {
+      SlotGroup<float> xs;
+      load_group(px, xs);
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const V x3[3] = {xs.v[3 * j], xs.v[3 * j + 1], xs.v[3 * j + 2]};
+        const V d[3] = {vsub(x2[0], x1[0]), vsub(x2[1], x1[1]), vsub(x2[2], x1[2])};
+        const V d2 = dot3(d, d);
+        dmin2 = fmin(dmin2, d2);
+        const V d_phi = vmul(dot3(d, tau), bond_rsqrt(d2));
+        const V e[3] = {vsub(x3[0], x2[0]), vsub(x3[1], x2[1]), vsub(x3[2], x2[2])};
+        tau[0] = vfma(e[2], Fs[1], vfma(vneg(e[1]), Fs[2], tau[0]));
+        tau[1] = vfma(e[0], Fs[2], vfma(vneg(e[2]), Fs[0], tau[1]));
+        tau[2] = vfma(e[1], Fs[0], vfma(vneg(e[0]), Fs[1], tau[2]));
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          Fs[i] = vsub(Fs[i], to_r<V>(pg[3 * j + i]));
+          x1[i] = x2[i];
+          x2[i] = x3[i];
+        }
+        xs.v[3 * j] = d_phi;
+      }
+      store_group(px, xs);
+    }
+  }
+  const bool bad = u < live && !(dmin2 >= static_cast<V>(1e-6) * xmax2);
+  bool redo = chain_any<W>(bad);
+  T* gr = grad_raw + chain * grad_stride;
+  if (!redo) {
+    // chain rule, one (sin, cos) pair per thread and iteration, as torsion_backward_xyz_vec_kernel
+    bool clamped = false;
+#pragma unroll 4
+    for (int k = u; k < St; k += NT) {
+      const V rs = to_r<V>(raw_s[2 * k]);
+      const V rc = to_r<V>(raw_s[2 * k + 1]);
+      const V n2raw = vfma(rs, rs, vmul(rc, rc));
+      clamped |= !(n2raw >= 1.0e-8f * 1.0e-8f);
+      const V rinv = torsion_rinv(torsion_norm2(rs, rc));
+      const V scale = vmul(X[3 * (k + 3)], vmul(rinv, rinv));
+      gr[2 * k] = from_r<T>(vmul(rc, scale));
+      gr[2 * k + 1] = from_r<T>(vneg(vmul(rs, scale)));
+    }
+    redo = chain_any<W>(clamped);
+  }
+  if (redo) {
+    // the recompute form of torsion_backward_kernel: float slots over the position region, the raw
+    // row and the grad row as staged (the fast form wrote neither)
+    chain_sync<W>();
+    ChainViews<T> cv;
+    cv.X = reinterpret_cast<R*>(xregion);
+    cv.row[0] = raw_s;
+    cv.G = Gh;
+    const StepRange range = step_range(u, (St + NT - 1) / NT, St);
+    torsion_backward_recompute<T, V, R, false>(cv, ex, consts, range, W);
+    chain_sync<W>();
+    write_pair_grads<T, R>(cv.X, gr, St, u, NT);
   }
 }
 

@@ -438,10 +438,18 @@ cufkb_torsion_constants torsion_constants(const std::vector<double>& c) {
   return out;
 }
 
-Tensor torsion_forward_impl(const Tensor& raw, const std::vector<double>& consts, const Shape& shape) {
+Tensor torsion_forward_impl(const Tensor& raw, const std::vector<double>& consts, const Shape& shape, Tensor* xyz32 = nullptr) {
   const c10::cuda::CUDAGuard guard(raw.device());
   const cufkb_torsion_constants c = torsion_constants(consts);
   Tensor xyz = torch::empty({shape.batch, shape.points, 3}, raw.options());
+  if (xyz32 != nullptr) {
+    // float16/bfloat16: the float32 positions as well, for the backward
+    *xyz32 = torch::empty({shape.batch, shape.points, 3}, raw.options().dtype(torch::kFloat32));
+    check_status(cufkb_torsion_forward_xyz32(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr(), xyz32->data_ptr<float>(),
+                                             shape.batch, shape.points, current_stream()),
+                 "torsion_pairs");
+    return xyz;
+  }
   check_status(cufkb_torsion_forward(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr(), shape.batch,
                                      shape.points, current_stream()),
                "torsion_pairs");
@@ -459,6 +467,14 @@ Tensor torsion_backward_xyz_impl(const Tensor& raw, const std::vector<double>& c
   const c10::cuda::CUDAGuard guard(raw.device());
   const cufkb_torsion_constants c = torsion_constants(consts);
   Tensor grad = pair_grad_like(raw, shape);
+  if (is_16bit(raw) && xyz.scalar_type() == torch::kFloat32) {
+    // float16/bfloat16 with the forward's float32 positions
+    check_status(cufkb_torsion_backward_from_xyz32(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr<float>(),
+                                                   grad_points.data_ptr(), grad.data_ptr(), grad.stride(0), shape.batch, shape.points,
+                                                   current_stream()),
+                 "torsion_pairs backward");
+    return grad;
+  }
   check_status(cufkb_torsion_backward_from_xyz(dtype_code(raw.scalar_type()), raw.data_ptr(), raw.stride(0), &c, xyz.data_ptr(),
                                                grad_points.data_ptr(), grad.data_ptr(), grad.stride(0), shape.batch, shape.points,
                                                current_stream()),
@@ -481,8 +497,10 @@ class TorsionAutograd : public torch::autograd::Function<TorsionAutograd> {
  public:
   static Tensor forward(AutogradContext* ctx, Tensor raw_pairs, std::vector<double> consts) {
     const Shape shape = check_pairs(raw_pairs);
-    Tensor xyz = torsion_forward_impl(raw_pairs, consts, shape);
-    ctx->save_for_backward({raw_pairs, xyz});
+    // float16/bfloat16 save the float32 positions instead, as the block wrapper does
+    Tensor xyz32;
+    Tensor xyz = torsion_forward_impl(raw_pairs, consts, shape, is_16bit(raw_pairs) ? &xyz32 : nullptr);
+    ctx->save_for_backward({raw_pairs, xyz32.defined() ? xyz32 : xyz});
     ctx->saved_data["consts"] = c10::IValue(consts);
     return xyz;
   }
@@ -591,6 +609,27 @@ Tensor torsion_backward(const Tensor& raw, const std::vector<double>& consts, co
   return torsion_backward_impl(raw, consts, grad_points, shape);
 }
 
+// float16/bfloat16: the torsion forward with its float32 positions, and the backward reading them
+std::vector<Tensor> torsion_forward_xyz32(const Tensor& raw, const std::vector<double>& consts) {
+  const Shape shape = check_pairs(raw);
+  TORCH_CHECK(is_16bit(raw), "torsion_forward_xyz32 supports float16 and bfloat16");
+  Tensor xyz32;
+  Tensor xyz = torsion_forward_impl(raw, consts, shape, &xyz32);
+  return {xyz, xyz32};
+}
+
+Tensor torsion_backward_from_xyz32(const Tensor& raw, const std::vector<double>& consts, const Tensor& xyz32, const Tensor& grad_points) {
+  const Shape shape = check_pairs(raw);
+  TORCH_CHECK(is_16bit(raw), "torsion_backward_from_xyz32 supports float16 and bfloat16");
+  check_like(grad_points, raw, "grad_points");
+  check_cuda_float(xyz32, "xyz32");
+  TORCH_CHECK(xyz32.scalar_type() == torch::kFloat32, "xyz32 must be float32");
+  TORCH_CHECK(xyz32.device() == raw.device(), "xyz32 must be on the same device as reference");
+  TORCH_CHECK(grad_points.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "grad_points must have shape (B, N, 3)");
+  TORCH_CHECK(xyz32.sizes() == torch::IntArrayRef({shape.batch, shape.points, 3}), "xyz32 must have shape (B, N, 3)");
+  return torsion_backward_xyz_impl(raw, consts, xyz32, grad_points, shape);
+}
+
 Tensor torsion_backward_from_xyz(const Tensor& raw, const std::vector<double>& consts, const Tensor& xyz, const Tensor& grad_points) {
   const Shape shape = check_pairs(raw);
   check_like(grad_points, raw, "grad_points");
@@ -634,5 +673,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("torsion_forward", &torsion_forward, "torsion forward kernel only");
   m.def("torsion_backward", &torsion_backward, "torsion backward kernel only");
   m.def("torsion_backward_from_xyz", &torsion_backward_from_xyz, "torsion backward kernel reading the forward's xyz");
+  m.def("torsion_forward_xyz32", &torsion_forward_xyz32, "16-bit torsion forward kernel writing float32 positions as well");
+  m.def("torsion_backward_from_xyz32", &torsion_backward_from_xyz32, "16-bit torsion backward kernel reading the forward's float32 positions");
   m.def("max_point_count", &cufkb_max_point_count);
 }

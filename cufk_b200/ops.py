@@ -23,7 +23,8 @@ Operators (namespace ``cufk_b200``):
   library) or, for float16/bfloat16, the float32 ``xyz32``;
 * ``torsion_reconstruct(raw_pairs, constants) -> xyz`` and ``torsion_backward(raw_pairs,
   constants, xyz, grad_xyz) -> grad_raw_pairs``, with ``constants`` the nine floats of
-  ``torsion.torsion_constants``.
+  ``torsion.torsion_constants``; ``torsion_reconstruct_xyz32`` is the float16/bfloat16 forward
+  that also returns the float32 positions its backward reads (as ``reconstruct_xyz32``).
 
 Python helpers with the public signatures: ``reconstruct`` (1-D single-chain inputs included; the
 16-bit types go through ``reconstruct_xyz32``, the kernels of the C++ wrapper) and
@@ -201,6 +202,9 @@ def _(raw_pairs, constants):
 @torch.library.custom_op("cufk_b200::torsion_backward", mutates_args=())
 def _torsion_backward_op(raw_pairs: Tensor, constants: list[float], xyz: Tensor, grad_xyz: Tensor) -> Tensor:
     # the gradient copies raw_pairs' strides (empty_strided_like, extension_utils.cuh:162-164)
+    if xyz.dtype != raw_pairs.dtype:
+        # float16/bfloat16 with the float32 positions of torsion_reconstruct_xyz32
+        return _C.torsion_backward_from_xyz32(raw_pairs, constants, xyz, grad_xyz.contiguous())
     return _C.torsion_backward_from_xyz(raw_pairs, constants, xyz, grad_xyz.contiguous())
 
 
@@ -224,7 +228,39 @@ def _torsion_grad(ctx, grad_xyz):
 _torsion_op.register_autograd(_torsion_grad, setup_context=_torsion_setup)
 
 
+@torch.library.custom_op("cufk_b200::torsion_reconstruct_xyz32", mutates_args=())
+def _torsion_xyz32_op(raw_pairs: Tensor, constants: list[float]) -> tuple[Tensor, Tensor]:
+    xyz, xyz32 = _C.torsion_forward_xyz32(raw_pairs, constants)
+    return xyz, xyz32
+
+
+@_torsion_xyz32_op.register_fake
+def _(raw_pairs, constants):
+    batch, points = _fake_pairs(raw_pairs)
+    torch._check(raw_pairs.dtype in (torch.float16, torch.bfloat16), lambda: "torsion_forward_xyz32 supports float16 and bfloat16")
+    return raw_pairs.new_empty((batch, points, 3)), raw_pairs.new_empty((batch, points, 3), dtype=torch.float32)
+
+
+def _torsion_xyz32_setup(ctx, inputs, output):
+    raw_pairs, constants = inputs
+    ctx.constants = constants
+    ctx.mark_non_differentiable(output[1])
+    ctx.save_for_backward(raw_pairs, output[1])
+
+
+def _torsion_xyz32_grad(ctx, grad_xyz, _grad_xyz32):
+    raw_pairs, xyz32 = ctx.saved_tensors
+    return _torsion_backward_op(raw_pairs, ctx.constants, xyz32, grad_xyz), None
+
+
+_torsion_xyz32_op.register_autograd(_torsion_xyz32_grad, setup_context=_torsion_xyz32_setup)
+
+
 def torsion(raw_pairs: Tensor, bond_lengths: tuple[float, float, float], bond_angles: tuple[float, float, float]) -> Tensor:
     """``compile_torsion(bond_lengths, bond_angles)(raw_pairs)`` through the
-    ``cufk_b200::torsion_reconstruct`` operator."""
-    return _torsion_op(raw_pairs, torsion_constants(tuple(bond_lengths), tuple(bond_angles)))
+    ``cufk_b200::torsion_reconstruct`` operator (16-bit types: ``torsion_reconstruct_xyz32``, the
+    kernels of the C++ wrapper)."""
+    consts = torsion_constants(tuple(bond_lengths), tuple(bond_angles))
+    if raw_pairs.dtype in (torch.float16, torch.bfloat16):
+        return _torsion_xyz32_op(raw_pairs, consts)[0]
+    return _torsion_op(raw_pairs, consts)

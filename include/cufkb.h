@@ -198,6 +198,18 @@ CUFKB_API int cufkb_torsion_backward_from_xyz(int dtype, const void* raw_pairs, 
                                     void* grad_raw_pairs, int64_t grad_row_stride, int64_t batch, int64_t points,
                                     cufkb_stream_t stream);
 
+/* float16/bfloat16 torsion forward that also writes its float32 positions (xyz32, (B, N, 3)), and
+ * the raw-pair gradients from them: as cufkb_block_forward_xyz32 / cufkb_block_backward_from_xyz32
+ * for the block path (a 16-bit position is too coarse for the bond directions the xyz form takes).
+ * Replace forward_default_impl<T> / backward_xyz_impl<T> (src/cufk/csrc/torsion.cu:387-411) for the
+ * 16-bit types; float16/bfloat16 only (CUFKB_ERROR_UNSUPPORTED_DTYPE otherwise). */
+CUFKB_API int cufkb_torsion_forward_xyz32(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                                void* xyz, float* xyz32, int64_t batch, int64_t points, cufkb_stream_t stream);
+
+CUFKB_API int cufkb_torsion_backward_from_xyz32(int dtype, const void* raw_pairs, int64_t raw_row_stride, const cufkb_torsion_constants* constants,
+                                      const float* xyz32, const void* grad_xyz, void* grad_raw_pairs, int64_t grad_row_stride,
+                                      int64_t batch, int64_t points, cufkb_stream_t stream);
+
 /* Chains of any length N >= 4 (no counterpart in the reference, which stops at
  * BLOCK_SCAN_MAX_POINT_COUNT = 2051 points and leaves longer chains to a scan it does not ship,
  * README.md:52).  A chain is split into balanced segments of at most 2048 steps, one CTA each;

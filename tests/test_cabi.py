@@ -223,3 +223,23 @@ def test_xyz32_entry_points_validation(lib):
     assert bwdp(F16, 16, 32, 48, None, None, None, 136, 130, 64, 80, 96, 112, 2, 20, 10, None) == MISALIGNED
     assert bwdp(F16, 16, 32, 48, None, None, None, 136, 128, 64, 80, 96, 112, 2, -1, 10, None) == SHAPE_LIMITS
     assert bwdp(F16, 16, 32, 48, None, None, None, 136, 128, 64, 80, 96, 112, 0, 0, 10, None) == SUCCESS
+
+
+def test_torsion_xyz32_entry_points_validation(lib):
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.cufkb_torsion_forward_xyz32.argtypes = [ctypes.c_int, vp, i64, ctypes.POINTER(TorsionConstants), vp, vp, i64, i64, vp]
+    lib.cufkb_torsion_backward_from_xyz32.argtypes = [ctypes.c_int, vp, i64, ctypes.POINTER(TorsionConstants), vp, vp, vp, i64, i64, i64, vp]
+    c = TorsionConstants()
+    f = lib.cufkb_torsion_forward_xyz32
+    b = lib.cufkb_torsion_backward_from_xyz32
+    assert f(F32, 16, 14, ctypes.byref(c), 64, 128, 2, 10, None) == 11  # float16/bfloat16 only
+    assert f(F16, 16, 14, ctypes.byref(c), 64, None, 2, 10, None) == NULL_POINTER
+    assert f(F16, 16, 14, None, 64, 128, 2, 10, None) == INVALID_VALUE
+    assert f(BF16, 16, -1, ctypes.byref(c), 64, 128, 2, 10, None) == BAD_STRIDE
+    assert f(BF16, 16, 14, ctypes.byref(c), 64, 130, 2, 10, None) == MISALIGNED
+    assert f(F16, 16, 14, ctypes.byref(c), 64, 128, 0, 10, None) == SUCCESS
+    assert b(F64, 16, 14, ctypes.byref(c), 128, 64, 80, 14, 2, 10, None) == 11
+    assert b(F16, 16, 14, ctypes.byref(c), None, 64, 80, 14, 2, 10, None) == NULL_POINTER
+    assert b(F16, 16, 14, ctypes.byref(c), 128, 64, 80, 13, 2, 10, None) == BAD_STRIDE  # rows of 14 values would overlap
+    assert b(BF16, 16, 14, ctypes.byref(c), 130, 64, 80, 14, 2, 10, None) == MISALIGNED
+    assert b(BF16, 16, 14, ctypes.byref(c), 128, 64, 80, 14, 2, 2052, None) == TOO_MANY_STEPS

@@ -70,16 +70,25 @@ def test_opcheck_torsion():
     torch.library.opcheck(torch.ops.cufk_b200.torsion_reconstruct.default, (raw, consts))
 
 
-def test_torsion_operator_matches_compile_torsion():
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16, torch.bfloat16])
+def test_torsion_operator_matches_compile_torsion(dtype):
     tin = nerf64.make_torsion_inputs(9, 130, seed=4)
     f = cufk.compile_torsion(nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES)
     outs = []
     for fn in (f, lambda r: ops.torsion(r, nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES)):
-        raw = tin["raw"].to(DEV, torch.float32).requires_grad_(True)
+        raw = tin["raw"].to(DEV, dtype).requires_grad_(True)
         xyz = fn(raw)
-        xyz.backward(tin["grad"].to(DEV, torch.float32))
+        xyz.backward(tin["grad"].to(DEV, dtype))
         outs.append((xyz.detach(), raw.grad))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_opcheck_torsion_xyz32(dtype):
+    tin = nerf64.make_torsion_inputs(5, 40, seed=2)
+    raw = tin["raw"].to(DEV, dtype).requires_grad_(True)
+    consts = [float(c) for c in cufk.torsion.torsion_constants(nerf64.BACKBONE_LENGTHS, nerf64.BACKBONE_ANGLES)]
+    torch.library.opcheck(torch.ops.cufk_b200.torsion_reconstruct_xyz32.default, (raw, consts))
 
 
 def test_compile_fullgraph_traces_through_the_operator():

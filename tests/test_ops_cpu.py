@@ -11,7 +11,7 @@ from torch._subclasses.fake_tensor import FakeTensorMode
 import cufk_b200 as cufk
 from cufk_b200 import ops
 
-OPS = ("reconstruct", "reconstruct_xyz32", "reconstruct_backward", "torsion_reconstruct", "torsion_backward")
+OPS = ("reconstruct", "reconstruct_xyz32", "reconstruct_backward", "torsion_reconstruct", "torsion_reconstruct_xyz32", "torsion_backward")
 
 
 def test_operators_registered():
