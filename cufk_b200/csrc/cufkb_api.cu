@@ -235,7 +235,8 @@ struct LaunchEnv {
 // have started (enter_after_previous_grid); for a small grid that hides the launch latency between
 // the two (B200, config-1 chains, forward + backward per step: 512 chains 12.5 -> 11.5 us, 1024
 // chains 16.5 -> 15.5 us), but the next kernel's CTAs, resident early and waiting, slowed larger
-// ones (2048 chains: 26.8 -> 29.1 us), which therefore launch plainly.
+// ones (2048 chains: 26.8 -> 29.1 us), which therefore launch plainly; the one exception is the
+// vector forward larger than one resident wave (vec_overlap).
 constexpr int kOverlapCtasPerSm = 8;
 
 // Launches `kernel` on `stream`; small grids (kOverlapCtasPerSm) allow programmatic dependent launch:
@@ -259,11 +260,10 @@ bool overlap_launch(uint64_t ctas) {
 bool prefetch_launch(int64_t batch, const cufkb::PackedLayout& packed) { return packed.offsets == nullptr && overlap_launch(uint64_t(batch)); }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
-  const uint64_t ctas = uint64_t(grid.x) * grid.y * grid.z;
+cudaError_t launch_kernel_as(bool overlap, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = overlap_launch(ctas) ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -272,6 +272,13 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// The same with the small-grid rule (overlap_launch) for the overlap.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  const uint64_t ctas = uint64_t(grid.x) * grid.y * grid.z;
+  return launch_kernel_as(overlap_launch(ctas), kernel, grid, block, smem, stream, std::forward<Args>(args)...);
 }
 
 // Device, kernel footprint, shared-memory opt-in and plan of one launch.
@@ -511,6 +518,29 @@ std::pair<int, int> vec_plan(int64_t batch, int points, int delta) {
   return {w, vec_items<Elem>(points, delta, w)};
 }
 
+// Whether a launch of family F with W warps per chain overlaps the previous kernel: small grids
+// (overlap_launch) in every family, and vector forwards larger than one resident wave.  Such a
+// forward's CTAs let the next kernel in as soon as the last wave has started, and its own CTAs,
+// let in early during the previous kernel's last wave, ask L2 for their input rows, which no
+// earlier kernel writes, before they wait (B200, config-1 chains, forward alone 21.7 -> 20.1 us,
+// step 47.3 -> 46.6 us; config 2: forward 31.1 -> 27.7 us).  The other families measured no faster
+// or slower that way (the xyz backward after a forward that one wave holds, 3072 chains: step
+// 37.4 -> 38.8 us; the torsion step at config 3: 150.5 -> 153.4 us).
+template <VecFamily F, typename T, int W>
+bool vec_overlap(int64_t batch, int points, int items) {
+  if (overlap_launch(uint64_t(batch))) return true;
+  if constexpr (F == kVecForwardFamily || F == kVecForwardPrefetchFamily) {
+    int dev = 0, sms = 0;
+    if (current_device(&dev) != 0) return false;
+    const DeviceCache* d = device_cache(dev);
+    if (d->error) return false;
+    sms = d->sm_count;
+    const int per_sm = vec_resident<kVecForwardFamily, T>(W, points, items) / W;
+    return per_sm > 0 && batch > int64_t(per_sm) * sms;
+  }
+  return false;
+}
+
 // Launches family F's kernel with W warps per chain: one CTA per chain.
 template <VecFamily F, typename T, int W, typename... Args>
 int launch_vec(int64_t batch, int points, int items, cudaStream_t stream, Args... args) {
@@ -518,7 +548,8 @@ int launch_vec(int64_t batch, int points, int items, cudaStream_t stream, Args..
   const size_t smem = vec_smem<F, T>(points, items);
   LaunchEnv env;
   if (int st = launch_env(&env, kernel, kernel_id(vec_kind(F, W), dtype_index<T>()), batch, points, smem)) return st;
-  if (cudaError_t e = launch_kernel(kernel, static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream, args...)) return fail_cuda(e);
+  const bool overlap = vec_overlap<F, T, W>(batch, points, items);
+  if (cudaError_t e = launch_kernel_as(overlap, kernel, static_cast<unsigned>(batch), cufkb::kWarp * W, smem, stream, args...)) return fail_cuda(e);
   return CUFKB_SUCCESS;
 }
 
@@ -538,7 +569,7 @@ int block_forward_vec(const void* L, const void* A, const void* D, const void* p
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
   return with_vec_warps(w, [&](auto wc) {
     constexpr int W = decltype(wc)::value;
-    if (prefetch_launch(batch, packed)) return launch_vec<kVecForwardPrefetchFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
+    if (packed.offsets == nullptr && vec_overlap<kVecForwardFamily, T, W>(batch, points, items)) return launch_vec<kVecForwardPrefetchFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
     return launch_vec<kVecForwardFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
   });
 }
