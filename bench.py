@@ -632,11 +632,19 @@ def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
         os.sched_setaffinity(0, before)
     out["host_cpus"] = f"{len(local)} GPU-local cores (NVML affinity)" if local else "unchanged (no NVML affinity)"
     node = numa_node_of(local if local else before)
-    ranks = dist.gather([node, out.pop("_h2d_gbs"), out.pop("_d2h_gbs")])
-    out["per_rank"] = [{"rank": r, "numa_node": int(v[0]), "h2d_gbs": round(v[1], 1), "d2h_gbs": round(v[2], 1)} for r, v in enumerate(ranks)]
+    ranks = dist.gather([node, out.pop("_h2d_gbs"), out.pop("_d2h_gbs"), out.pop("_duplex_ms")])
+    out["per_rank"] = [
+        {"rank": r, "numa_node": int(v[0]), "h2d_gbs": round(v[1], 1), "d2h_gbs": round(v[2], 1), "copy_floor_ms": round(v[3], 4)}
+        for r, v in enumerate(ranks)
+    ]
+    floor = max(v[3] for v in ranks)
+    out["copy_floor_ms"] = round(floor, 4)
+    out["of_copy_floor"] = round(floor / out["ms_per_step"], 3)
     out["ceiling_note"] = (
-        "each step moves h2d_bytes_per_step + d2h_bytes_per_step per rank over its PCIe link; the copy-only "
-        "rates above bound the e2e step at max(h2d / h2d_gbs, d2h / d2h_gbs) when the two directions overlap"
+        "each step moves h2d_bytes_per_step + d2h_bytes_per_step per rank over its PCIe link; h2d_gbs / d2h_gbs "
+        "are each direction alone, copy_floor_ms one step's copy-in and copy-out issued together on two streams "
+        "(both directions at once, as the e2e loop overlaps them), the slowest rank's; of_copy_floor = "
+        "copy_floor_ms / ms_per_step"
     )
     return out
 
@@ -645,8 +653,9 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     """The metric through the public API with host buffers: every step copies the inputs and the
     grad host->device from pinned memory, runs ``cufk_b200.reconstruct`` + ``backward`` and copies
     xyz and the three gradients device->host.  Copy-in, compute and copy-out are on three streams,
-    so that one step's results travel back while the next step's inputs arrive (both PCIe
-    directions at once), as a caller streaming batches would run it."""
+    and alternate steps use two device input sets, so that one step's results travel back while
+    the next step's inputs arrive (both PCIe directions at once), as a caller streaming batches
+    would run it."""
     b = host["lengths"].shape[0]
     pinned = {k: v.pin_memory() for k, v in host.items()}
     outs = {
@@ -657,26 +666,33 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     }
     h2d = sum(v.numel() * v.element_size() for v in pinned.values())
     d2h = sum(v.numel() * v.element_size() for v in outs.values())
-    buf = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    # two device input sets, used by alternate steps: a step's copy-in waits only for the compute two
+    # steps back, so it runs while the previous step computes and copies out
+    bufs = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
+    buf = bufs[0]
     s_in, s_run, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-    free = [None]
+    free = [None, None]
+    turn = [0]
 
     def step():
+        slot = turn[0]
+        turn[0] ^= 1
+        b = bufs[slot]
         with torch.cuda.stream(s_in):
-            if free[0] is not None:
-                s_in.wait_event(free[0])  # the previous compute has read the buffer
+            if free[slot] is not None:
+                s_in.wait_event(free[slot])  # the compute that last read this input set is done
             for k in ("lengths", "angles", "dihedrals", "grad"):
-                buf[k].copy_(pinned[k], non_blocking=True)
+                b[k].copy_(pinned[k], non_blocking=True)
             copied = torch.cuda.Event()
             copied.record(s_in)
         with torch.cuda.stream(s_run):
             s_run.wait_event(copied)
-            L, A, D = (buf[k].detach().requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
+            L, A, D = (b[k].detach().requires_grad_(True) for k in ("lengths", "angles", "dihedrals"))
             xyz = cufk.reconstruct(L, A, D)
-            xyz.backward(buf["grad"])
+            xyz.backward(b["grad"])
             done = torch.cuda.Event()
             done.record(s_run)
-            free[0] = done
+            free[slot] = done
         with torch.cuda.stream(s_out):
             s_out.wait_event(done)
             for src, key in ((xyz.detach(), "xyz"), (L.grad, "gl"), (A.grad, "ga"), (D.grad, "gd")):
@@ -732,7 +748,33 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
             for k, v in outs.items():
                 v.copy_(dev_out[k], non_blocking=True)
 
+    def duplex_ms():
+        # one step's copy-in and copy-out issued together on two streams (both PCIe directions at
+        # once, as the e2e loop overlaps them): the copy floor of an e2e step
+        reps = 10
+        for _ in range(2):
+            copy_once("h2d")
+            copy_once("d2h")
+        torch.cuda.synchronize()
+        dist.barrier()
+        cur = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        for _ in range(reps):
+            with torch.cuda.stream(s_in):
+                copy_once("h2d")
+            with torch.cuda.stream(s_out):
+                copy_once("d2h")
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
     h2d_gbs, d2h_gbs = copy_rate("h2d"), copy_rate("d2h")
+    both_ms = duplex_ms()
     return {
         "value": global_batch * args.points / (ms * 1e-3),
         "unit": "atoms/s",
@@ -740,9 +782,10 @@ def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
         "d2h_bytes_per_step": d2h,
         "ms_per_step": ms,
         "steps": steps,
-        "path": "cufk_b200.reconstruct + autograd backward; pinned host buffers, copies inside the timed region; copy-in / compute / copy-out on three streams",
+        "path": "cufk_b200.reconstruct + autograd backward; pinned host buffers, copies inside the timed region; copy-in / compute / copy-out on three streams, two device input sets alternating",
         "_h2d_gbs": h2d_gbs,
         "_d2h_gbs": d2h_gbs,
+        "_duplex_ms": both_ms,
     }
 
 
