@@ -239,10 +239,6 @@ struct LaunchEnv {
 // vector forward larger than one resident wave (vec_overlap).
 constexpr int kOverlapCtasPerSm = 8;
 
-// Launches `kernel` on `stream`; small grids (kOverlapCtasPerSm) allow programmatic dependent launch:
-// the kernel may then be scheduled while the previous kernel in the stream finishes, and, like every
-// kernel of this library, waits for that kernel's completion (enter_after_previous_grid) before
-// touching global memory.  Returns the launch's own error.
 // Whether a grid of `ctas` CTAs is launched to overlap the previous kernel (kOverlapCtasPerSm).
 bool overlap_launch(uint64_t ctas) {
   int dev = 0, sms = 148;
@@ -259,6 +255,10 @@ bool overlap_launch(uint64_t ctas) {
 // chains 17.03 -> 15.70 us).
 bool prefetch_launch(int64_t batch, const cufkb::PackedLayout& packed) { return packed.offsets == nullptr && overlap_launch(uint64_t(batch)); }
 
+// Launches `kernel` on `stream`, with programmatic dependent launch when `overlap`: the kernel may
+// then be scheduled while the previous kernel in the stream finishes, and, like every kernel of this
+// library, waits for that kernel's completion (enter_after_previous_grid) before touching global
+// memory.  Returns the launch's own error.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_kernel_as(bool overlap, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
   cudaLaunchAttribute attr[1];
@@ -518,26 +518,31 @@ std::pair<int, int> vec_plan(int64_t batch, int points, int delta) {
   return {w, vec_items<Elem>(points, delta, w)};
 }
 
+// Whether a (B, N) vector forward of `batch` chains needs more than one resident wave.  Such a
+// forward is launched overlapping the previous kernel, in the prefetching instantiation: it lets the
+// next kernel in as soon as its last wave has started, and its own CTAs, let in early during the
+// previous kernel's last wave, ask L2 for their input rows, which no earlier kernel writes, before
+// they wait (B200, config 1: forward alone 21.7 -> 20.0 us, step 47.2 -> 45.7 us; config 2 fp32:
+// forward 31.1 -> 27.7 us, step 78.2 -> 77.0 us).  The other families measured no faster or slower
+// that way (the xyz backward after a forward that one wave holds, 3072 chains: step 37.4 -> 38.8 us;
+// the torsion step at config 3: 150.5 -> 153.4 us), and packed forwards, which do not prefetch,
+// keep the small-grid rule.
+template <typename T, int W>
+bool forward_beyond_one_wave(int64_t batch, int points, int items) {
+  int dev = 0;
+  if (current_device(&dev) != 0) return false;
+  const DeviceCache* d = device_cache(dev);
+  if (d->error) return false;
+  const int per_sm = vec_resident<kVecForwardFamily, T>(W, points, items) / W;
+  return per_sm > 0 && batch > int64_t(per_sm) * d->sm_count;
+}
+
 // Whether a launch of family F with W warps per chain overlaps the previous kernel: small grids
-// (overlap_launch) in every family, and vector forwards larger than one resident wave.  Such a
-// forward's CTAs let the next kernel in as soon as the last wave has started, and its own CTAs,
-// let in early during the previous kernel's last wave, ask L2 for their input rows, which no
-// earlier kernel writes, before they wait (B200, config-1 chains, forward alone 21.7 -> 20.1 us,
-// step 47.3 -> 46.6 us; config 2: forward 31.1 -> 27.7 us).  The other families measured no faster
-// or slower that way (the xyz backward after a forward that one wave holds, 3072 chains: step
-// 37.4 -> 38.8 us; the torsion step at config 3: 150.5 -> 153.4 us).
+// (overlap_launch) in every family, and prefetching forwards beyond one resident wave.
 template <VecFamily F, typename T, int W>
 bool vec_overlap(int64_t batch, int points, int items) {
   if (overlap_launch(uint64_t(batch))) return true;
-  if constexpr (F == kVecForwardFamily || F == kVecForwardPrefetchFamily) {
-    int dev = 0, sms = 0;
-    if (current_device(&dev) != 0) return false;
-    const DeviceCache* d = device_cache(dev);
-    if (d->error) return false;
-    sms = d->sm_count;
-    const int per_sm = vec_resident<kVecForwardFamily, T>(W, points, items) / W;
-    return per_sm > 0 && batch > int64_t(per_sm) * sms;
-  }
+  if constexpr (F == kVecForwardPrefetchFamily) return forward_beyond_one_wave<T, W>(batch, points, items);
   return false;
 }
 
@@ -569,7 +574,7 @@ int block_forward_vec(const void* L, const void* A, const void* D, const void* p
   const ChainGeometry geo{static_cast<int>(batch), points, points - 3, items, packed};
   return with_vec_warps(w, [&](auto wc) {
     constexpr int W = decltype(wc)::value;
-    if (packed.offsets == nullptr && vec_overlap<kVecForwardFamily, T, W>(batch, points, items)) return launch_vec<kVecForwardPrefetchFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
+    if (packed.offsets == nullptr && vec_overlap<kVecForwardPrefetchFamily, T, W>(batch, points, items)) return launch_vec<kVecForwardPrefetchFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
     return launch_vec<kVecForwardFamily, T, W>(batch, points, items, stream, args, static_cast<T*>(xyz), geo);
   });
 }
