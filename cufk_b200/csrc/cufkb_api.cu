@@ -236,7 +236,7 @@ struct LaunchEnv {
 // the two (B200, config-1 chains, forward + backward per step: 512 chains 12.5 -> 11.5 us, 1024
 // chains 16.5 -> 15.5 us), but the next kernel's CTAs, resident early and waiting, slowed larger
 // ones (2048 chains: 26.8 -> 29.1 us), which therefore launch plainly; the one exception is the
-// vector forward larger than one resident wave (vec_overlap).
+// (B, N) vector forward larger than one resident wave (forward_beyond_one_wave).
 constexpr int kOverlapCtasPerSm = 8;
 
 // Whether a grid of `ctas` CTAs is launched to overlap the previous kernel (kOverlapCtasPerSm).
