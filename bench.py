@@ -633,13 +633,7 @@ def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
     out["host_cpus"] = f"{len(local)} GPU-local cores (NVML affinity)" if local else "unchanged (no NVML affinity)"
     node = numa_node_of(local if local else before)
     ranks = dist.gather([node, out.pop("_h2d_gbs"), out.pop("_d2h_gbs"), out.pop("_duplex_ms")])
-    out["per_rank"] = [
-        {"rank": r, "numa_node": int(v[0]), "h2d_gbs": round(v[1], 1), "d2h_gbs": round(v[2], 1), "copy_floor_ms": round(v[3], 4)}
-        for r, v in enumerate(ranks)
-    ]
-    floor = max(v[3] for v in ranks)
-    out["copy_floor_ms"] = round(floor, 4)
-    out["of_copy_floor"] = round(floor / out["ms_per_step"], 3)
+    out.update(e2e_rank_summary(ranks, out["ms_per_step"]))
     out["ceiling_note"] = (
         "each step moves h2d_bytes_per_step + d2h_bytes_per_step per rank over its PCIe link; h2d_gbs / d2h_gbs "
         "are each direction alone, copy_floor_ms one step's copy-in and copy-out issued together on two streams "
@@ -647,6 +641,21 @@ def run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:
         "copy_floor_ms / ms_per_step"
     )
     return out
+
+
+def e2e_rank_summary(ranks: list[list[float]], ms_per_step: float) -> dict:
+    """The e2e record's per-rank part from every rank's gathered [NUMA node, H2D GB/s, D2H GB/s,
+    copy floor ms]: `per_rank`, the slowest rank's `copy_floor_ms`, and `of_copy_floor` (that floor
+    over the e2e step time, the max over ranks)."""
+    floor = max(v[3] for v in ranks)
+    return {
+        "per_rank": [
+            {"rank": r, "numa_node": int(v[0]), "h2d_gbs": round(v[1], 1), "d2h_gbs": round(v[2], 1), "copy_floor_ms": round(v[3], 4)}
+            for r, v in enumerate(ranks)
+        ],
+        "copy_floor_ms": round(floor, 4),
+        "of_copy_floor": round(floor / ms_per_step, 3),
+    }
 
 
 def _run_e2e(cufk, host, dev, args, dist: Dist, global_batch: int) -> dict:

@@ -100,3 +100,16 @@ def test_rank_inputs_weak_and_strong():
         assert torch.equal(torch.cat([p[k] for p, _ in parts]), whole[k])
     # one rank: the same either way
     assert torch.equal(bench.rank_inputs(make, 5, "weak", 1, 0)[0]["grad"], bench.rank_inputs(make, 5, "strong", 1, 0)[0]["grad"])
+
+
+def test_e2e_rank_summary_two_ranks():
+    # the per-rank part of bench.py's e2e record, as rank 0 builds it from two ranks' gathered values
+    import bench
+
+    ranks = [[0.0, 54.8, 55.7, 1.70], [1.0, 50.2, 51.0, 1.80]]
+    s = bench.e2e_rank_summary(ranks, 1.9)
+    assert [p["rank"] for p in s["per_rank"]] == [0, 1]
+    assert [p["numa_node"] for p in s["per_rank"]] == [0, 1]
+    assert s["per_rank"][1]["h2d_gbs"] == 50.2 and s["per_rank"][1]["copy_floor_ms"] == 1.8
+    assert s["copy_floor_ms"] == 1.8
+    assert s["of_copy_floor"] == round(1.8 / 1.9, 3)
